@@ -1,0 +1,92 @@
+"""Build libb200gemm.so (the C-ABI library) and the per-experiment executables.
+
+Every CUDA translation unit is compiled for sm_100a only
+(``-gencode arch=compute_100a,code=sm_100a``), the B200 counterpart of the
+reference's ``-gencode=arch=compute_90a,code=sm_90a`` (CMakeLists.txt:21).
+Objects go to ``hopper-lab_b200/_build/``; the shared library to
+``hopper-lab_b200/lib/`` (in-tree, so it travels with the repository snapshot).
+
+Usage: python hopper-lab_b200/build.py [--force] [-j N]
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+BUILD = PKG / "_build"
+LIB = PKG / "lib"
+BIN = PKG / "bin"
+
+NVCC = os.environ.get("NVCC", shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVFLAGS = ARCH + [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xcompiler",
+    "-fPIC",
+    f"-I{ROOT / 'include'}",
+    f"-I{CSRC}",
+]
+
+LIB_SOURCES = ["b200gemm.cu", "inst_f16.cu", "inst_bf16.cu", "inst_e4m3.cu", "quant.cu"]
+HEADERS = ["sm100_ptx.cuh", "gemm_sm100.cuh", "gemm_launch.cuh"]
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(d.exists() and d.stat().st_mtime > t for d in deps)
+
+
+def _run(cmd: list[str]) -> None:
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(" ".join(cmd) + "\n" + r.stdout + r.stderr)
+        raise RuntimeError(f"build step failed: {cmd[-1]}")
+
+
+def _headers() -> list[Path]:
+    return [CSRC / h for h in HEADERS] + [ROOT / "include" / "b200gemm.h"]
+
+
+def build_library(force: bool = False, jobs: int = 8) -> Path:
+    BUILD.mkdir(exist_ok=True)
+    LIB.mkdir(exist_ok=True)
+    objs = []
+    todo = []
+    for src in LIB_SOURCES:
+        s = CSRC / src
+        o = BUILD / (s.stem + ".o")
+        objs.append(o)
+        if force or _stale(o, [s] + _headers()):
+            todo.append([NVCC, *NVFLAGS, "-c", str(s), "-o", str(o)])
+    with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
+        list(ex.map(_run, todo))
+    so = LIB / "libb200gemm.so"
+    if force or todo or _stale(so, objs):
+        _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", str(so), *map(str, objs)])
+    return so
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-j", type=int, default=8)
+    a = ap.parse_args()
+    so = build_library(force=a.force, jobs=a.j)
+    print(so)
+
+
+if __name__ == "__main__":
+    main()

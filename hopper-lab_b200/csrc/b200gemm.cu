@@ -1,0 +1,345 @@
+// b200gemm.cu — the C ABI (include/b200gemm.h): validation, tensor-map encoding,
+// variant selection and launch. Host code only; kernels live in inst_*.cu.
+//
+// Reference interfaces replaced here:
+//   make_tmap_h / make_tmap_f           src/05_gemm/gemm_ws.cu:162-199
+//   make_tmap_fp8                       src/07_fp8/gemm_fp8.cu:145-168
+//   launch_config<S,tma> / dispatch     src/05_gemm/gemm_ws.cu:201-235
+//   persistent launch_config (grid = min(tiles, SMs*occ))
+//                                       src/08_persistent/gemm_fp8_persist.cu:222-242
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/b200gemm.h"
+#include "gemm_launch.cuh"
+
+namespace {
+
+using b200::GemmCfg;
+using b200::KParams;
+using b200::LaunchPlan;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+std::mutex g_mu;
+EncodeTiledFn g_encode = nullptr;
+uint32_t* g_status[64] = {nullptr};
+int g_sm_count[64] = {0};
+int g_cc_major[64] = {0};
+
+constexpr uint64_t kDefaultWaitNs = 1000000000ull;  // 1 s per wait
+constexpr int kDefaultGroupM = 8;
+
+int resolve_encode() {
+  if (g_encode) return B200_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e =
+      cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return B200_ERR_CUDA;
+  g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  return B200_OK;
+}
+
+// Per-device one-time set-up: driver entry point, SM count, status word.
+int device_setup(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return B200_ERR_CUDA;
+  *dev_out = dev;
+  if (g_status[dev]) return B200_OK;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_status[dev]) return B200_OK;
+  int rc = resolve_encode();
+  if (rc != B200_OK) return rc;
+  int sms = 0, major = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return B200_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return B200_ERR_CUDA;
+  uint32_t* st = nullptr;
+  if (cudaMalloc(&st, 256) != cudaSuccess) return B200_ERR_CUDA;
+  if (cudaMemset(st, 0, 256) != cudaSuccess) return B200_ERR_CUDA;
+  g_sm_count[dev] = sms;
+  g_cc_major[dev] = major;
+  g_status[dev] = st;
+  return B200_OK;
+}
+
+int elem_bytes(int dt) {
+  switch (dt) {
+    case B200_DT_F16:
+    case B200_DT_BF16: return 2;
+    case B200_DT_E4M3: return 1;
+    case B200_DT_F32: return 4;
+    default: return 0;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 2D tensor map over a row-major [rows x cols] matrix with leading dimension ld
+// (elements), box [box_rows x box_cols], 128-byte swizzle. Out-of-range boxes are
+// zero-filled on load and clipped on store, which is what makes ragged M/N/K work.
+int encode_2d(CUtensorMap* m, const void* ptr, int dt, uint64_t rows, uint64_t cols, uint64_t ld,
+              uint32_t box_rows, uint32_t box_cols) {
+  CUtensorMapDataType t;
+  switch (dt) {
+    case B200_DT_F16: t = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; break;
+    case B200_DT_BF16: t = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; break;
+    case B200_DT_E4M3: t = CU_TENSOR_MAP_DATA_TYPE_UINT8; break;
+    case B200_DT_F32: t = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; break;
+    default: return B200_ERR_INVALID_ARG;
+  }
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstride[1] = {ld * static_cast<uint64_t>(elem_bytes(dt))};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  std::memset(m, 0, sizeof(*m));
+  CUresult r = g_encode(m, t, 2, const_cast<void*>(ptr), gdim, gstride, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TMAP;
+}
+
+struct VariantShape {
+  int cg, sched;
+  uint32_t tile_m, tile_n, max_stages, default_stages;
+};
+
+// Tile facts per variant; every variant uses BN = 256 and BM = 128 per CTA.
+int variant_shape(int variant, int ab, VariantShape* vs) {
+  const bool fp8 = (ab == B200_DT_E4M3);
+  (void)fp8;
+  switch (variant) {
+    case B200_VARIANT_1CTA:
+    case B200_VARIANT_PERSISTENT:
+      vs->cg = 1;
+      vs->sched = b200::SCHED_STATIC;
+      vs->max_stages = GemmCfg<b200::DT_F16, b200::DT_F16, 1, 0>::MAX_STAGES;
+      break;
+    case B200_VARIANT_CLC:
+      vs->cg = 1;
+      vs->sched = b200::SCHED_CLC;
+      vs->max_stages = GemmCfg<b200::DT_F16, b200::DT_F16, 1, 1>::MAX_STAGES;
+      break;
+    case B200_VARIANT_2CTA:
+      vs->cg = 2;
+      vs->sched = b200::SCHED_STATIC;
+      vs->max_stages = GemmCfg<b200::DT_F16, b200::DT_F16, 2, 0>::MAX_STAGES;
+      break;
+    default: return B200_ERR_INVALID_ARG;
+  }
+  // Stage bytes do not depend on the element type (one 128-byte K atom per row).
+  if (vs->max_stages > 8) vs->max_stages = 8;
+  vs->default_stages = vs->max_stages;
+  vs->tile_m = 128u * vs->cg;
+  vs->tile_n = 256u;
+  return B200_OK;
+}
+
+int pick_variant(const B200GemmArgs* a, int sms) {
+  const int64_t pair_tiles = ((a->M + 255) / 256) * ((a->N + 255) / 256);
+  // The pair variant halves each SM's B traffic; use it once there is at least
+  // half a wave of pair tiles. Small problems keep 1-CTA tiles for parallelism.
+  if (a->M >= 256 && pair_tiles * 2 >= sms) return B200_VARIANT_2CTA;
+  const int64_t tiles = ((a->M + 127) / 128) * ((a->N + 255) / 256);
+  if (tiles > sms) return B200_VARIANT_PERSISTENT;
+  return B200_VARIANT_1CTA;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_gemm_abi_version(void) { return B200GEMM_ABI_VERSION; }
+
+const char* b200_gemm_strerror(int code) {
+  switch (code) {
+    case B200_OK: return "ok";
+    case B200_ERR_INVALID_ARG: return "invalid argument (null pointer, dtype or variant)";
+    case B200_ERR_SHAPE: return "invalid shape or leading dimension";
+    case B200_ERR_ALIGN: return "pointer or row stride is not 16-byte aligned";
+    case B200_ERR_TMAP: return "tensor-map encoding failed";
+    case B200_ERR_LAUNCH: return "kernel launch failed";
+    case B200_ERR_DEVICE_TIMEOUT: return "a bounded device wait timed out";
+    case B200_ERR_UNSUPPORTED: return "unsupported dtype/variant or device (needs sm_100)";
+    case B200_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown error code";
+  }
+}
+
+int b200_gemm_variant_info(int32_t variant, int32_t ab_dtype, int32_t* tile_m, int32_t* tile_n,
+                           int32_t* max_stages, int32_t* default_stages) {
+  if (ab_dtype != B200_DT_F16 && ab_dtype != B200_DT_BF16 && ab_dtype != B200_DT_E4M3)
+    return B200_ERR_INVALID_ARG;
+  VariantShape vs;
+  int rc = variant_shape(variant, ab_dtype, &vs);
+  if (rc != B200_OK) return rc;
+  if (tile_m) *tile_m = static_cast<int32_t>(vs.tile_m);
+  if (tile_n) *tile_n = static_cast<int32_t>(vs.tile_n);
+  if (max_stages) *max_stages = static_cast<int32_t>(vs.max_stages);
+  if (default_stages) *default_stages = static_cast<int32_t>(vs.default_stages);
+  return B200_OK;
+}
+
+// Argument checks that need no GPU (shared by b200_gemm and b200_gemm_pick_variant).
+static int validate(const B200GemmArgs* a) {
+  if (!a) return B200_ERR_INVALID_ARG;
+  if (a->ab_dtype != B200_DT_F16 && a->ab_dtype != B200_DT_BF16 && a->ab_dtype != B200_DT_E4M3)
+    return B200_ERR_INVALID_ARG;
+  if (a->c_dtype != B200_DT_F16 && a->c_dtype != B200_DT_BF16 && a->c_dtype != B200_DT_F32)
+    return B200_ERR_INVALID_ARG;
+  if (a->variant < B200_VARIANT_AUTO || a->variant > B200_VARIANT_CLC) return B200_ERR_INVALID_ARG;
+  if (a->M < 0 || a->N < 0 || a->K < 0) return B200_ERR_SHAPE;
+  // TMA coordinates are int32 and the tile counters are uint32.
+  const int64_t lim = (int64_t(1) << 31) - 1;
+  if (a->M > lim || a->N > lim || a->K > lim) return B200_ERR_SHAPE;
+  if (a->group_m < 0 || a->stages < 0) return B200_ERR_INVALID_ARG;
+  if (a->M == 0 || a->N == 0) return B200_OK;
+  if (a->lda < a->K || a->ldb < a->K || a->ldc < a->N) return B200_ERR_SHAPE;
+  if (a->lda < 1 || a->ldb < 1) return B200_ERR_SHAPE;
+  if (!a->C) return B200_ERR_INVALID_ARG;
+  if (a->K > 0 && (!a->A || !a->B)) return B200_ERR_INVALID_ARG;
+  const int eb = elem_bytes(a->ab_dtype), ec = elem_bytes(a->c_dtype);
+  if (!aligned16(a->C) || (a->K > 0 && (!aligned16(a->A) || !aligned16(a->B))))
+    return B200_ERR_ALIGN;
+  if ((a->lda * eb) % 16 || (a->ldb * eb) % 16 || (a->ldc * ec) % 16) return B200_ERR_ALIGN;
+  // TMA global strides must stay below 2^40 bytes.
+  if (a->lda * eb >= (int64_t(1) << 40) || a->ldb * eb >= (int64_t(1) << 40) ||
+      a->ldc * ec >= (int64_t(1) << 40))
+    return B200_ERR_SHAPE;
+  if ((a->scale_a && (reinterpret_cast<uintptr_t>(a->scale_a) & 3u)) ||
+      (a->scale_b && (reinterpret_cast<uintptr_t>(a->scale_b) & 3u)))
+    return B200_ERR_ALIGN;
+  return B200_OK;
+}
+
+int b200_gemm_pick_variant(const B200GemmArgs* args) {
+  int rc = validate(args);
+  if (rc != B200_OK) return rc;
+  if (args->variant != B200_VARIANT_AUTO) return args->variant;
+  int dev = 0;
+  rc = device_setup(&dev);
+  if (rc != B200_OK) return rc;
+  return pick_variant(args, g_sm_count[dev]);
+}
+
+int b200_gemm(const B200GemmArgs* args, void* stream_v) {
+  int rc = validate(args);
+  if (rc != B200_OK) return rc;
+  const B200GemmArgs& a = *args;
+  if (a.M == 0 || a.N == 0) return B200_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  int dev = 0;
+  rc = device_setup(&dev);
+  if (rc != B200_OK) return rc;
+  if (g_cc_major[dev] != 10) return B200_ERR_UNSUPPORTED;
+  const int ec = elem_bytes(a.c_dtype);
+
+  if (a.K == 0) {  // empty reduction: C = 0
+    cudaError_t e = cudaMemset2DAsync(a.C, size_t(a.ldc) * ec, 0, size_t(a.N) * ec, size_t(a.M), stream);
+    return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  }
+
+  const int variant = (a.variant == B200_VARIANT_AUTO) ? pick_variant(&a, g_sm_count[dev]) : a.variant;
+  VariantShape vs;
+  rc = variant_shape(variant, a.ab_dtype, &vs);
+  if (rc != B200_OK) return rc;
+  const uint32_t stages = a.stages ? uint32_t(a.stages) : vs.default_stages;
+  if (stages < 2 || stages > vs.max_stages) return B200_ERR_INVALID_ARG;
+
+  const uint32_t bk = (a.ab_dtype == B200_DT_E4M3) ? 128u : 64u;
+  const uint32_t cd_cols = 128u / uint32_t(ec);
+
+  alignas(64) CUtensorMap tA, tB, tC;
+  rc = encode_2d(&tA, a.A, a.ab_dtype, uint64_t(a.M), uint64_t(a.K), uint64_t(a.lda), 128u, bk);
+  if (rc != B200_OK) return rc;
+  rc = encode_2d(&tB, a.B, a.ab_dtype, uint64_t(a.N), uint64_t(a.K), uint64_t(a.ldb),
+                 vs.tile_n / uint32_t(vs.cg), bk);
+  if (rc != B200_OK) return rc;
+  rc = encode_2d(&tC, a.C, a.c_dtype, uint64_t(a.M), uint64_t(a.N), uint64_t(a.ldc), 32u, cd_cols);
+  if (rc != B200_OK) return rc;
+
+  KParams kp;
+  std::memset(&kp, 0, sizeof(kp));
+  kp.M = uint32_t(a.M);
+  kp.N = uint32_t(a.N);
+  kp.K = uint32_t(a.K);
+  kp.m_tiles = uint32_t((a.M + vs.tile_m - 1) / vs.tile_m);
+  kp.n_tiles = uint32_t((a.N + vs.tile_n - 1) / vs.tile_n);
+  const uint64_t tiles = uint64_t(kp.m_tiles) * kp.n_tiles;
+  if (tiles > 0x7fffffffull / 2) return B200_ERR_SHAPE;
+  kp.num_tiles = uint32_t(tiles);
+  kp.k_blocks = uint32_t((a.K + bk - 1) / bk);
+  kp.stages = stages;
+  kp.group_m = a.group_m ? uint32_t(a.group_m) : uint32_t(kDefaultGroupM);
+  kp.fault_inject = a.fault_inject ? 1u : 0u;
+  kp.scale_a = a.scale_a;
+  kp.scale_b = a.scale_b;
+  kp.status = g_status[dev];
+  kp.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kDefaultWaitNs;
+
+  const uint32_t sms = uint32_t(g_sm_count[dev]);
+  uint32_t grid = 0;
+  switch (variant) {
+    case B200_VARIANT_1CTA:
+    case B200_VARIANT_CLC: grid = kp.num_tiles; break;
+    case B200_VARIANT_PERSISTENT: grid = kp.num_tiles < sms ? kp.num_tiles : sms; break;
+    case B200_VARIANT_2CTA: {
+      const uint32_t pairs = sms / 2;
+      grid = 2u * (kp.num_tiles < pairs ? kp.num_tiles : pairs);
+      break;
+    }
+    default: return B200_ERR_INVALID_ARG;
+  }
+
+  LaunchPlan lp;
+  lp.a = &tA;
+  lp.b = &tB;
+  lp.c = &tC;
+  lp.kp = kp;
+  lp.grid = grid;
+  lp.stream = stream;
+  // smem_bytes() depends only on the stage size, identical for every dtype.
+  lp.smem = (vs.cg == 1) ? GemmCfg<b200::DT_F16, b200::DT_F16, 1, 0>::smem_bytes(stages)
+                         : GemmCfg<b200::DT_F16, b200::DT_F16, 2, 0>::smem_bytes(stages);
+
+  cudaError_t e;
+  switch (a.ab_dtype) {
+    case B200_DT_F16: e = b200::launch_f16(a.c_dtype, vs.cg, vs.sched, lp); break;
+    case B200_DT_BF16: e = b200::launch_bf16(a.c_dtype, vs.cg, vs.sched, lp); break;
+    default: e = b200::launch_e4m3(a.c_dtype, vs.cg, vs.sched, lp); break;
+  }
+  if (e == cudaErrorNotSupported) return B200_ERR_UNSUPPORTED;
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return B200_ERR_LAUNCH;
+  }
+  return B200_OK;
+}
+
+int b200_gemm_status(void* stream_v, int clear, uint32_t* bits) {
+  int dev = 0;
+  int rc = device_setup(&dev);
+  if (rc != B200_OK) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return B200_ERR_CUDA;
+  uint32_t v = 0;
+  if (cudaMemcpy(&v, g_status[dev], sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return B200_ERR_CUDA;
+  if (clear && v) {
+    if (cudaMemset(g_status[dev], 0, sizeof(uint32_t)) != cudaSuccess) return B200_ERR_CUDA;
+  }
+  if (bits) *bits = v;
+  return v ? B200_ERR_DEVICE_TIMEOUT : B200_OK;
+}
+
+}  // extern "C"

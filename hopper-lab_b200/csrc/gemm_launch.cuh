@@ -1,0 +1,76 @@
+// gemm_launch.cuh — launch wrapper shared by the per-dtype instantiation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "gemm_sm100.cuh"
+
+namespace b200 {
+
+struct LaunchPlan {
+  const CUtensorMap* a;
+  const CUtensorMap* b;
+  const CUtensorMap* c;
+  KParams kp;
+  uint32_t grid;   // CTAs (a multiple of CG)
+  uint32_t smem;   // dynamic shared memory bytes
+  cudaStream_t stream;
+};
+
+template <int AB, int CD, int CG, int SCHED>
+cudaError_t launch_gemm(const LaunchPlan& lp) {
+  auto kern = gemm_tcgen05_kernel<AB, CD, CG, SCHED>;
+  // The opt-in shared-memory size is a per-function, per-device attribute.
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(GemmCfg<AB, CD, CG, SCHED>::MAX_SMEM));
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(lp.grid, 1, 1);
+  cfg.blockDim = dim3(GemmCfg<AB, CD, CG, SCHED>::NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = lp.smem;
+  cfg.stream = lp.stream;
+  cudaLaunchAttribute attr[1];
+  if (CG == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, *lp.a, *lp.b, *lp.c, lp.kp);
+}
+
+// One dispatch entry per (AB, CD, variant) — defined in the instantiation units.
+cudaError_t launch_f16(int cd, int cg, int sched, const LaunchPlan& lp);
+cudaError_t launch_bf16(int cd, int cg, int sched, const LaunchPlan& lp);
+cudaError_t launch_e4m3(int cd, int cg, int sched, const LaunchPlan& lp);
+
+#define B200_DEFINE_DISPATCH(NAME, AB)                                                  \
+  cudaError_t NAME(int cd, int cg, int sched, const LaunchPlan& lp) {                   \
+    if (cg == 1 && sched == SCHED_STATIC) {                                              \
+      if (cd == DT_F16) return launch_gemm<AB, DT_F16, 1, SCHED_STATIC>(lp);             \
+      if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, 1, SCHED_STATIC>(lp);           \
+      if (cd == DT_F32) return launch_gemm<AB, DT_F32, 1, SCHED_STATIC>(lp);             \
+    } else if (cg == 1 && sched == SCHED_CLC) {                                          \
+      if (cd == DT_F16) return launch_gemm<AB, DT_F16, 1, SCHED_CLC>(lp);                \
+      if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, 1, SCHED_CLC>(lp);              \
+      if (cd == DT_F32) return launch_gemm<AB, DT_F32, 1, SCHED_CLC>(lp);                \
+    } else if (cg == 2 && sched == SCHED_STATIC) {                                       \
+      if (cd == DT_F16) return launch_gemm<AB, DT_F16, 2, SCHED_STATIC>(lp);             \
+      if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, 2, SCHED_STATIC>(lp);           \
+      if (cd == DT_F32) return launch_gemm<AB, DT_F32, 2, SCHED_STATIC>(lp);             \
+    }                                                                                    \
+    return cudaErrorNotSupported;                                                        \
+  }
+
+}  // namespace b200

@@ -1,0 +1,442 @@
+// gemm_sm100.cuh — warp-specialised tcgen05 GEMM for B200 (sm_100a).
+//
+//   C[M,N] = scale_a * scale_b * (A[M,K] · B[N,K]^T),  fp32 accumulation in TMEM
+//
+// Layout contract ("TN"), identical to the reference's GEMM experiments
+// (src/05_gemm/gemm_ws.cu:258-265, src/07_fp8/gemm_fp8.cu:246-253): A is M×K
+// row-major, B is stored N×K (K contiguous), C is M×N row-major. Leading
+// dimensions are free (lda ≥ K, ldb ≥ K, ldc ≥ N, 16-byte multiples).
+//
+// What each reference kernel becomes here:
+//   gemm_ws_kernel   (src/05_gemm/gemm_ws.cu:56)   -> CG=1, one tile per CTA
+//   gemm_ws_cluster  (src/06_cluster/gemm_ws_cluster.cu:50) -> CG=2, the CTA pair
+//                    shares B through cta_group::2 (each CTA loads half of it)
+//   gemm_fp8_kernel  (src/07_fp8/gemm_fp8.cu:48)   -> AB = e4m3, kind::f8f6f4,
+//                    per-tensor fp32 scales fused in the epilogue
+//   gemm_fp8_persist (src/08_persistent/gemm_fp8_persist.cu:68) -> SCHED_STATIC
+//                    (grid = resident CTAs, tile += grid, group-M order)
+//   gemm_fp8_bn128   (src/08_persistent/gemm_fp8_bn128.cu:73, dynamic queue)
+//                    -> SCHED_CLC: hardware cluster-launch-control work stealing
+//                    replaces the global atomic tile counter
+//
+// CTA = 256 threads, 8 warps:
+//   warp 0      TMA producer (one lane): A/B k-blocks into an S-stage smem ring
+//   warp 1      TMEM owner + MMA issuer (one lane of the leader CTA)
+//   warp 2      CLC scheduler (one lane; SCHED_CLC only)
+//   warp 3      idle
+//   warps 4-7   epilogue: TMEM -> registers -> (scale, narrow) -> swizzled smem ->
+//               TMA store; warp 4+q drains TMEM lanes 32q..32q+31
+// Two fp32 accumulators of BN columns each live in TMEM, so the epilogue of tile t
+// overlaps the main loop of tile t+1.
+#pragma once
+
+#include "sm100_ptx.cuh"
+
+namespace b200 {
+
+enum : int { DT_F16 = 0, DT_BF16 = 1, DT_E4M3 = 2, DT_F32 = 3 };
+enum : int { SCHED_STATIC = 0, SCHED_CLC = 1 };
+
+// Bits OR-ed into the device status word when a bounded wait gives up.
+enum : uint32_t {
+  ST_PRODUCER_EMPTY = 1u << 0,
+  ST_MMA_FULL = 1u << 1,
+  ST_MMA_TMEM_EMPTY = 1u << 2,
+  ST_EPI_TMEM_FULL = 1u << 3,
+  ST_SCHED = 1u << 4,
+  ST_DRAIN = 1u << 5,
+  ST_ABORTED = 1u << 31,
+};
+
+struct KParams {
+  uint32_t M, N, K;
+  uint32_t m_tiles;    // ceil(M / (128*CG))
+  uint32_t n_tiles;    // ceil(N / BN)
+  uint32_t num_tiles;  // m_tiles * n_tiles
+  uint32_t k_blocks;   // ceil(K / BK)
+  uint32_t stages;     // smem ring depth (runtime, ≤ the kernel's maximum)
+  uint32_t group_m;    // group-M swizzle width (≥ 1)
+  uint32_t fault_inject;  // test hook: 1 = the producer issues no loads
+  const float* scale_a;   // device, per-tensor, may be null (= 1)
+  const float* scale_b;
+  uint32_t* status;       // device status word, may be null
+  uint64_t wait_ns;       // bound of every mbarrier wait
+};
+
+// Linear tile id -> (block-row, block-col) in group-M order. Same mapping as the
+// reference's tile_to_bmn (src/08_persistent/gemm_fp8_persist.cu:56-66): groups of
+// G block-rows, block-row fastest inside a group; G = 1 is plain row-wave order.
+__host__ __device__ inline void tile_to_bmn(uint32_t tile, uint32_t num_bm, uint32_t num_bn,
+                                            uint32_t G, uint32_t& bm, uint32_t& bn) {
+  const uint32_t per_group = G * num_bn;
+  const uint32_t g = tile / per_group;
+  const uint32_t first_bm = g * G;
+  const uint32_t rem = num_bm - first_bm;
+  const uint32_t gsize = rem < G ? rem : G;
+  const uint32_t t = tile - g * per_group;
+  bm = first_bm + t % gsize;
+  bn = t / gsize;
+}
+
+template <int AB, int CD, int CG, int SCHED>
+struct GemmCfg {
+  static constexpr int BM = 128;                       // rows of C per CTA
+  static constexpr int BN = 256;                       // columns of C per tile (MMA N)
+  static constexpr int KIND = (AB == DT_E4M3) ? 1 : 0; // 0 kind::f16, 1 kind::f8f6f4
+  static constexpr int AB_BYTES = (AB == DT_E4M3) ? 1 : 2;
+  static constexpr int BK = 128 / AB_BYTES;            // one 128-byte swizzle atom of K
+  static constexpr int KSTEPS = 4;                     // 32-byte MMA K-steps per k-block
+  static constexpr int B_ROWS = BN / CG;               // rows of B held by each CTA
+  static constexpr uint32_t A_STAGE = BM * 128;        // bytes
+  static constexpr uint32_t B_STAGE = B_ROWS * 128;
+  static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
+  static constexpr int CD_BYTES = (CD == DT_F32) ? 4 : 2;
+  static constexpr int EPI_COLS = 128 / CD_BYTES;      // C columns per 128-byte chunk
+  static constexpr int EPI_CHUNKS = BN / EPI_COLS;
+  static constexpr uint32_t EPI_BUF = 32 * 128;        // 32 rows × 128 bytes
+  static constexpr uint32_t EPI_BYTES = 4 * 2 * EPI_BUF;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;        // two fp32 accumulators
+  static constexpr uint32_t MMA_M = BM * CG;
+  static constexpr uint32_t IDESC =
+      idesc_f32acc(AB == DT_BF16 ? 1u : 0u, AB == DT_BF16 ? 1u : 0u, MMA_M, BN);
+  static constexpr uint32_t MAX_SMEM = 232448;         // 227 KB opt-in per CTA
+  static constexpr uint32_t BAR_BYTES = 256;
+  static constexpr uint32_t ALIGN_SLACK = 1024;
+  static constexpr uint32_t MAX_STAGES =
+      (MAX_SMEM - EPI_BYTES - BAR_BYTES - ALIGN_SLACK) / STAGE;
+  static constexpr uint32_t DEFAULT_STAGES = MAX_STAGES;
+  static constexpr uint32_t NUM_THREADS = 256;
+  static constexpr uint32_t SCHED_CONSUMERS = 6;       // producer + MMA + 4 epilogue warps
+
+  static uint32_t smem_bytes(uint32_t stages) {
+    return stages * STAGE + EPI_BYTES + BAR_BYTES + ALIGN_SLACK;
+  }
+  static_assert(TMEM_COLS <= 512, "TMEM has 512 columns");
+  static_assert(!(SCHED == SCHED_CLC && CG == 2), "CLC scheduling is built for 1-CTA tiles");
+};
+
+template <int AB, int CD, int CG, int SCHED>
+__global__ void __launch_bounds__(256, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const KParams p) {
+  using Cfg = GemmCfg<AB, CD, CG, SCHED>;
+  extern __shared__ uint8_t smem_raw[];
+
+  // ---- shared-memory carve-up (1024-byte aligned for SWIZZLE_128B) ----
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw);
+  const uint32_t S = p.stages;
+  const uint32_t sA = base;
+  const uint32_t sB = base + S * Cfg::A_STAGE;
+  const uint32_t sEpi = base + S * Cfg::STAGE;
+  const uint32_t sBar = sEpi + Cfg::EPI_BYTES;
+  uint8_t* bar_ptr = base_ptr + (sBar - base);
+  // 8-byte barriers: full[8], empty[8], tfull[2], tempty[2], sfull[2], sempty[2], done
+  const uint32_t bar_full = sBar;
+  const uint32_t bar_empty = sBar + 64;
+  const uint32_t bar_tfull = sBar + 128;
+  const uint32_t bar_tempty = sBar + 144;
+  const uint32_t bar_sfull = sBar + 160;
+  const uint32_t bar_sempty = sBar + 176;
+  const uint32_t bar_done = sBar + 192;
+  const uint32_t clc_resp = sBar + 208;                 // 2 × 16 B
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 240);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(bar_ptr + 244);
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+
+  if (warp == 0 && lane == 0) {
+    for (uint32_t s = 0; s < S; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (uint32_t a = 0; a < 2; ++a) {
+      mbar_init(bar_tfull + 8 * a, 1);
+      mbar_init(bar_tempty + 8 * a, 4 * CG);
+      mbar_init(bar_sfull + 8 * a, 1);
+      mbar_init(bar_sempty + 8 * a, Cfg::SCHED_CONSUMERS);
+    }
+    mbar_init(bar_done, 1);
+    *abort_flag = 0u;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc<CG>(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish<CG>();
+  }
+  tc_fence_before();
+  if constexpr (CG == 2) cluster_sync(); else __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto fail = [&](uint32_t code) {
+    *abort_flag = 1u;
+    if (p.status) atomicOr(p.status, code | ST_ABORTED);
+  };
+
+  // ---- tile sequence shared by every role ----
+  // SCHED_STATIC: cluster c takes tiles c, c + G, c + 2G, ... (G = clusters in grid)
+  // SCHED_CLC   : tile = blockIdx.x first, then whatever try_cancel returns
+  const uint32_t first_tile = blockIdx.x / CG;
+  const uint32_t tile_stride = gridDim.x / CG;
+
+  // Reads the next tile from the CLC ring (consumer side). Returns false when the
+  // schedule is exhausted or the CTA aborted.
+  uint32_t sched_slot = 0, sched_phase = 0;
+  auto clc_next = [&](uint32_t& tile, bool single_lane) -> bool {
+    bool ok = mbar_wait(bar_sfull + 8 * sched_slot, sched_phase, p.wait_ns, abort_flag);
+    if (!ok) { fail(ST_SCHED); return false; }
+    uint32_t x = 0;
+    const bool got = clc_decode(clc_resp + 16 * sched_slot, x);
+    if (single_lane) mbar_arrive(bar_sempty + 8 * sched_slot);
+    if (++sched_slot == 2) { sched_slot = 0; sched_phase ^= 1; }
+    tile = x;
+    return got;
+  };
+
+  if (warp == 0) {
+    // =============================== TMA producer ===============================
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      const uint64_t hint = policy_evict_normal();
+      const uint32_t leader_full0 = (CG == 2) ? mapa_shared(bar_full, 0) : bar_full;
+      if (!p.fault_inject) {
+        uint32_t tile = first_tile;
+        bool more = tile < p.num_tiles;
+        while (more && ok) {
+          uint32_t bm, bn;
+          tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
+          const int32_t a_row = int32_t((bm * CG + rank) * Cfg::BM);
+          const int32_t b_row = int32_t(bn * Cfg::BN + rank * Cfg::B_ROWS);
+          for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+            if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, p.wait_ns, abort_flag)) {
+              fail(ST_PRODUCER_EMPTY);
+              ok = false;
+              break;
+            }
+            const int32_t kx = int32_t(kb * Cfg::BK);
+            if constexpr (CG == 1) {
+              mbar_arrive_expect_tx(bar_full + 8 * stage, Cfg::STAGE);
+              tma_load_2d(sA + stage * Cfg::A_STAGE, &tmA, kx, a_row, bar_full + 8 * stage, hint);
+              tma_load_2d(sB + stage * Cfg::B_STAGE, &tmB, kx, b_row, bar_full + 8 * stage, hint);
+            } else {
+              if (rank == 0) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * Cfg::STAGE);
+              const uint32_t lf = leader_full0 + 8 * stage;
+              tma_load_2d_pair(sA + stage * Cfg::A_STAGE, &tmA, kx, a_row, lf, hint);
+              tma_load_2d_pair(sB + stage * Cfg::B_STAGE, &tmB, kx, b_row, lf, hint);
+            }
+            ++issued;
+            if (++stage == S) { stage = 0; phase ^= 1u; }
+          }
+          if (!ok) break;
+          if constexpr (SCHED == SCHED_CLC) {
+            more = clc_next(tile, true);
+          } else {
+            tile += tile_stride;
+            more = tile < p.num_tiles;
+          }
+        }
+      }
+      if (!ok || *abort_flag) {
+        // Error path: wait (bounded) for the loads this CTA still has in flight so
+        // that no TMA write lands after the CTA's shared memory is released.
+        if constexpr (CG == 1) {
+          const uint32_t first = issued > S ? issued - S : 0u;
+          for (uint32_t i = first; i < issued; ++i) {
+            const uint32_t s = i % S, par = (i / S) & 1u;
+            if (!mbar_wait_bounded(bar_full + 8 * s, par, p.wait_ns)) break;
+          }
+        } else {
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 50000ull) { }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ============================ MMA issuer (leader) ============================
+    if (lane == 0 && rank == 0) {
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      uint32_t tile = first_tile;
+      bool more = tile < p.num_tiles;
+      while (more && ok) {
+        if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, p.wait_ns, abort_flag)) {
+          fail(ST_MMA_TMEM_EMPTY);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::BN;
+        for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(bar_full + 8 * stage, phase, p.wait_ns, abort_flag)) {
+            fail(ST_MMA_FULL);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + stage * Cfg::A_STAGE;
+          const uint32_t b0 = sB + stage * Cfg::B_STAGE;
+#pragma unroll
+          for (uint32_t k = 0; k < Cfg::KSTEPS; ++k) {
+            umma<CG, Cfg::KIND>(d_tmem, sdesc_k_sw128(a0 + 32u * k), sdesc_k_sw128(b0 + 32u * k),
+                                Cfg::IDESC, (kb | k) != 0u ? 1u : 0u);
+          }
+          umma_commit<CG>(bar_empty + 8 * stage);
+          if constexpr (CG == 2) umma_commit<CG>(mapa_shared(bar_empty + 8 * stage, 1));
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit<CG>(bar_tfull + 8 * acc);
+        if constexpr (CG == 2) umma_commit<CG>(mapa_shared(bar_tfull + 8 * acc, 1));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        if constexpr (SCHED == SCHED_CLC) {
+          more = clc_next(tile, true);
+        } else {
+          tile += tile_stride;
+          more = tile < p.num_tiles;
+        }
+      }
+      // Every MMA this thread issued must retire before TMEM is released.
+      umma_commit<CG>(bar_done);
+      if (!mbar_wait_bounded(bar_done, 0, p.wait_ns)) fail(ST_DRAIN);
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ============================== CLC scheduler ==============================
+    if constexpr (SCHED == SCHED_CLC) {
+      if (lane == 0 && first_tile < p.num_tiles) {
+        uint32_t slot = 0, ph = 0;
+        while (true) {
+          if (!mbar_wait(bar_sempty + 8 * slot, ph ^ 1u, p.wait_ns, abort_flag)) {
+            fail(ST_SCHED);
+            break;
+          }
+          mbar_arrive_expect_tx(bar_sfull + 8 * slot, 16);
+          clc_try_cancel(clc_resp + 16 * slot, bar_sfull + 8 * slot);
+          if (!mbar_wait(bar_sfull + 8 * slot, ph, p.wait_ns, abort_flag)) {
+            fail(ST_SCHED);
+            break;
+          }
+          uint32_t x;
+          if (!clc_decode(clc_resp + 16 * slot, x)) break;  // grid exhausted: stop asking
+          if (++slot == 2) { slot = 0; ph ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ================================ epilogue ================================
+    const uint32_t q = warp - 4;  // TMEM lane quarter == warp id % 4
+    float scale = 1.0f;
+    if (p.scale_a) scale *= __ldg(p.scale_a);
+    if (p.scale_b) scale *= __ldg(p.scale_b);
+    const uint32_t my_buf0 = sEpi + q * 2 * Cfg::EPI_BUF;
+    const uint32_t leader_tempty0 = (CG == 2) ? mapa_shared(bar_tempty, 0) : bar_tempty;
+    uint32_t acc = 0, acc_phase = 0, buf = 0;
+    uint32_t tile = first_tile;
+    bool more = tile < p.num_tiles;
+    while (more) {
+      uint32_t bm, bn;
+      tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
+      uint32_t okw = 0;
+      if (lane == 0) okw = mbar_wait(bar_tfull + 8 * acc, acc_phase, p.wait_ns, abort_flag) ? 1u : 0u;
+      okw = __shfl_sync(0xffffffffu, okw, 0);
+      if (!okw) {
+        if (lane == 0) fail(ST_EPI_TMEM_FULL);
+        break;
+      }
+      tc_fence_after();
+      const int32_t row0 = int32_t((bm * CG + rank) * Cfg::BM + 32 * q);
+      const uint32_t t_row = tmem_base + ((32u * q) << 16) + acc * Cfg::BN;
+#pragma unroll 1
+      for (uint32_t c = 0; c < Cfg::EPI_CHUNKS; ++c) {
+        uint32_t w[32];
+        if constexpr (Cfg::CD_BYTES == 4) {
+          uint32_t r[32];
+          tmem_ld_x32(t_row + c * Cfg::EPI_COLS, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(r[i]) * scale);
+        } else {
+          uint32_t r0[32], r1[32];
+          tmem_ld_x32(t_row + c * Cfg::EPI_COLS, r0);
+          tmem_ld_x32(t_row + c * Cfg::EPI_COLS + 32, r1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float x0 = __uint_as_float(r0[2 * i]) * scale;
+            const float x1 = __uint_as_float(r0[2 * i + 1]) * scale;
+            const float y0 = __uint_as_float(r1[2 * i]) * scale;
+            const float y1 = __uint_as_float(r1[2 * i + 1]) * scale;
+            if constexpr (CD == DT_BF16) {
+              w[i] = pack_bf16x2(x0, x1);
+              w[16 + i] = pack_bf16x2(y0, y1);
+            } else {
+              w[i] = pack_f16x2(x0, x1);
+              w[16 + i] = pack_f16x2(y0, y1);
+            }
+          }
+        }
+        if (c == Cfg::EPI_CHUNKS - 1) {
+          // All TMEM reads of this accumulator are done: hand it back to the MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 1) mbar_arrive(bar_tempty + 8 * acc);
+            else mbar_arrive_cluster(leader_tempty0 + 8 * acc);
+          }
+        }
+        // Staging buffer `buf` was last read by the TMA store committed two chunks ago.
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        const uint32_t sb = my_buf0 + buf * Cfg::EPI_BUF;
+        const uint32_t row_addr = sb + lane * 128u;
+#pragma unroll
+        for (uint32_t j = 0; j < 8; ++j) {
+          st_shared_v4(row_addr + ((j ^ (lane & 7u)) << 4), w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                       w[4 * j + 3]);
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          // Boxes that start past the end of C (ragged M/N) are skipped; a box that
+          // straddles the edge is clipped by the TMA unit.
+          const uint32_t col0 = bn * Cfg::BN + c * Cfg::EPI_COLS;
+          if (uint32_t(row0) < p.M && col0 < p.N) tma_store_2d(&tmC, sb, int32_t(col0), row0);
+          bulk_commit();
+        }
+        buf ^= 1u;
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      if constexpr (SCHED == SCHED_CLC) {
+        uint32_t nt = 0;
+        bool got = false;
+        if (lane == 0) got = clc_next(nt, true);
+        got = __shfl_sync(0xffffffffu, got ? 1u : 0u, 0) != 0u;
+        tile = __shfl_sync(0xffffffffu, nt, 0);
+        more = got;
+      } else {
+        tile += tile_stride;
+        more = tile < p.num_tiles;
+      }
+    }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
+
+  // ---- teardown: every role has left its loop; release TMEM ----
+  tc_fence_before();
+  if constexpr (CG == 2) cluster_sync(); else __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<CG>(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace b200

@@ -1,0 +1,120 @@
+/* b200gemm.h — C ABI of the B200 (sm_100a) dense GEMM library, libb200gemm.so.
+ *
+ * The reference (TheManWhoIsStupid/Hopper-lab) has no library and no FFI: each
+ * experiment carries its kernel launcher in an anonymous namespace,
+ *   launch_config<S,...>(tmap_a, tmap_b, tmap_d, D, M, N, K[, group_m])   and
+ *   dispatch(stages, flag, ...)
+ * (src/05_gemm/gemm_ws.cu:201-235, src/07_fp8/gemm_fp8.cu:188-215,
+ *  src/08_persistent/gemm_fp8_persist.cu:222-270, src/08_persistent/gemm_fp8_bn128.cu:256-311).
+ * b200_gemm() replaces all of those launchers with one entry point: it encodes the
+ * tensor maps itself (the reference's make_tmap_h / make_tmap_fp8 / make_tmap_f,
+ * src/05_gemm/gemm_ws.cu:162-199), validates shape and alignment, and launches on
+ * the caller's stream.
+ *
+ * Conventions
+ *   - Layout "TN": A is M x K row-major, B is N x K row-major (K contiguous), C is
+ *     M x N row-major; C = scale_a * scale_b * A . B^T with fp32 accumulation.
+ *   - All pointers are device pointers of the current CUDA device.
+ *   - Never exits the process (the reference's launchers exit on error,
+ *     include/common/errors.h:8-16); every failure is a negative return code.
+ *   - Stream-ordered and asynchronous; thread-safe; no allocation on the hot path
+ *     (the per-device status word is allocated once, on the first call on a device).
+ *   - Device-side waits are bounded: a protocol failure sets the device status
+ *     word, which b200_gemm_status() reads back as B200_ERR_DEVICE_TIMEOUT.
+ */
+#ifndef B200GEMM_H_
+#define B200GEMM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200GEMM_ABI_VERSION 1
+
+/* element types */
+enum {
+  B200_DT_F16 = 0,  /* IEEE binary16                              */
+  B200_DT_BF16 = 1, /* bfloat16                                   */
+  B200_DT_E4M3 = 2, /* fp8 e4m3 (OCP "fn": no inf, max 448)       */
+  B200_DT_F32 = 3   /* output only                                */
+};
+
+/* kernel variants (the reference experiment each one succeeds) */
+enum {
+  B200_VARIANT_AUTO = 0,       /* library picks                                        */
+  B200_VARIANT_1CTA = 1,       /* one 128x256 tile per CTA    (05_gemm gemm_ws)        */
+  B200_VARIANT_2CTA = 2,       /* cta_group::2 pair, 256x256 tile, persistent
+                                  static schedule            (06_cluster gemm_ws_cluster)*/
+  B200_VARIANT_PERSISTENT = 3, /* 1-CTA, grid = SM count, static group-M schedule
+                                                              (08_persistent persist)  */
+  B200_VARIANT_CLC = 4         /* 1-CTA, cluster-launch-control work stealing
+                                                              (08_persistent bn128 dyn)*/
+};
+
+/* return codes */
+enum {
+  B200_OK = 0,
+  B200_ERR_INVALID_ARG = -1,   /* null args / pointers, unknown dtype or variant      */
+  B200_ERR_SHAPE = -2,         /* negative or oversize dims, ld < K or ld < N          */
+  B200_ERR_ALIGN = -3,         /* pointer or row stride not 16-byte aligned            */
+  B200_ERR_TMAP = -4,          /* cuTensorMapEncodeTiled rejected a descriptor         */
+  B200_ERR_LAUNCH = -5,        /* CUDA launch / attribute error                        */
+  B200_ERR_DEVICE_TIMEOUT = -6,/* a bounded device wait gave up (see b200_gemm_status) */
+  B200_ERR_UNSUPPORTED = -7,   /* dtype/variant combination not built, or not sm_100   */
+  B200_ERR_CUDA = -8           /* other CUDA runtime error                             */
+};
+
+typedef struct B200GemmArgs {
+  int32_t ab_dtype;        /* B200_DT_F16 | B200_DT_BF16 | B200_DT_E4M3 (A and B)        */
+  int32_t c_dtype;         /* B200_DT_F16 | B200_DT_BF16 | B200_DT_F32                   */
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc;   /* elements; lda >= K, ldb >= K, ldc >= N                     */
+  const void* A;           /* M x lda                                                    */
+  const void* B;           /* N x ldb                                                    */
+  void* C;                 /* M x ldc                                                    */
+  const float* scale_a;    /* device fp32 scalar or NULL (1.0)                           */
+  const float* scale_b;    /* device fp32 scalar or NULL (1.0)                           */
+  int32_t variant;         /* B200_VARIANT_*                                             */
+  int32_t group_m;         /* group-M swizzle width, 0 = library default                 */
+  int32_t stages;          /* smem ring depth, 0 = library default                       */
+  int32_t fault_inject;    /* 0 in production; 1 = test hook: producer issues no loads,
+                              so the bounded waits must report a device timeout          */
+  uint64_t wait_limit_ns;  /* bound of each device wait, 0 = library default (1 s)       */
+} B200GemmArgs;
+
+/* Launch C = scale_a*scale_b*A.B^T on `stream` (a cudaStream_t, NULL = legacy default). */
+int b200_gemm(const B200GemmArgs* args, void* stream);
+
+/* Human-readable text of a return code. */
+const char* b200_gemm_strerror(int code);
+
+/* Synchronise `stream`, then read (and clear when `clear` != 0) the device status
+ * word of the current device. Returns B200_OK, B200_ERR_DEVICE_TIMEOUT (and stores
+ * the raw bits in *bits when bits != NULL) or B200_ERR_CUDA. */
+int b200_gemm_status(void* stream, int clear, uint32_t* bits);
+
+/* Library facts: variant tile shape and stage limits, for hosts and tests.
+ * Returns B200_OK or B200_ERR_INVALID_ARG. */
+int b200_gemm_variant_info(int32_t variant, int32_t ab_dtype, int32_t* tile_m, int32_t* tile_n,
+                           int32_t* max_stages, int32_t* default_stages);
+
+/* The variant B200_VARIANT_AUTO resolves to for this problem on the current device. */
+int b200_gemm_pick_variant(const B200GemmArgs* args);
+
+/* Per-tensor e4m3 quantiser on the device: *scale = amax(|x|)/448 (1 when all
+ * x == 0) and q[i] = e4m3_rn_satfinite(x[i] / *scale). Device pointers: x (fp32,
+ * 16-byte aligned), q (n bytes, 8-byte aligned), scale (one fp32). Replaces the
+ * reference's host-side `quantize` (src/07_fp8/gemm_fp8.cu:182-186), which casts
+ * without a scale. Stream-ordered; returns B200_OK or a negative code. */
+int b200_quantize_e4m3(const float* x, int64_t n, void* q, float* scale, void* stream);
+
+/* ABI version (B200GEMM_ABI_VERSION). */
+int b200_gemm_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200GEMM_H_ */

@@ -1,0 +1,262 @@
+"""GPU parity tests: the tcgen05 GEMM (through the C ABI) against the CPU oracle.
+
+Each case mirrors a CHECK block of the reference or a BASELINE config:
+- reference CHECK blocks (fp32 C, the reference's own tolerances):
+  fp16 512x512x256 seeds 601/602, S in {2,3,4}, x3 reps (src/05_gemm/gemm_ws.cu:246-286);
+  e4m3 512x512x256 seeds 901/902 (src/07_fp8/gemm_fp8.cu:234-268);
+  persistent e4m3 512 and 2048x2048x256 seeds 1001/1002, G in {1,8}
+  (src/08_persistent/gemm_fp8_persist.cu:282-318);
+  dynamic-queue e4m3 seeds 2001/2002 (src/08_persistent/gemm_fp8_bn128.cu:323-351);
+- BASELINE configs 1-5 (f16/bf16/e4m3 in, f16/bf16 out), full checks where the
+  oracle is fast and seeded row bands at 8192;
+- edge cases: ragged M/N/K, padded leading dimensions, tiny shapes, K = 0;
+- the bounded-wait failure path (fault_inject) and the on-device quantiser.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from gemm_check import (TOL_16, TOL_E4M3, compare, make_inputs, out_to_f32, reference,
+                        sample_bands, to_device)
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+ALL_VARIANTS = ["1cta", "persistent", "clc", "2cta"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    yield
+    torch.cuda.synchronize()
+
+
+def _run(b200, inp, variant, out_dtype, reps=1, **kw):
+    a, b, sa, sb = to_device(inp, torch)
+    outs = []
+    for _ in range(reps):
+        c = torch.full((inp["M"], inp["N"]), float("nan"),
+                       dtype={"f16": torch.float16, "bf16": torch.bfloat16,
+                              "f32": torch.float32}[out_dtype], device="cuda")
+        b200.gemm(a, b, c, scale_a=sa, scale_b=sb, variant=variant, **kw)
+        outs.append(c)
+    torch.cuda.synchronize()
+    rc, bits = b200.status()
+    assert rc == 0, f"device status {bits:#x}"
+    return [out_to_f32(c, torch) for c in outs]
+
+
+# ------------------------------------------------------------ reference CHECK blocks
+@pytest.mark.parametrize("variant", ALL_VARIANTS)
+@pytest.mark.parametrize("stages", [2, 3, 4])
+def test_ref_check_fp16_512(b200, oracle, variant, stages):
+    """gemm_ws CHECK: 512x512x256 fp16, seeds 601/602, fp32 C, 1e-3/1e-3, x3."""
+    inp = make_inputs(oracle, 512, 512, 256, "f16", 601, 602)
+    ref = reference(oracle, inp)
+    for got in _run(b200, inp, variant, "f32", reps=3, stages=stages):
+        r = oracle.check_close(got, ref, 1e-3, 1e-3)
+        assert r.mismatches == 0 and np.isfinite(got).all(), (r.max_abs_err, r.max_rel_err)
+
+
+@pytest.mark.parametrize("variant", ALL_VARIANTS)
+def test_ref_check_fp8_512(b200, oracle, variant):
+    """gemm_fp8 CHECK: 512x512x256 e4m3 (unscaled), seeds 901/902, fp32 C, 3e-2, x3."""
+    inp = make_inputs(oracle, 512, 512, 256, "e4m3", 901, 902)
+    ref = reference(oracle, inp)
+    for got in _run(b200, inp, variant, "f32", reps=3):
+        r = oracle.check_close(got, ref, 3e-2, 3e-2)
+        assert r.mismatches == 0 and np.isfinite(got).all(), (r.max_abs_err, r.max_rel_err)
+
+
+@pytest.mark.parametrize("shape", [(512, 512, 256), (2048, 2048, 256)])
+@pytest.mark.parametrize("group_m", [1, 8])
+@pytest.mark.parametrize("variant,stages", [("persistent", 2), ("persistent", 4), ("clc", 4),
+                                            ("2cta", 6)])
+def test_ref_check_fp8_persistent(b200, oracle, shape, group_m, variant, stages):
+    """gemm_fp8_persist CHECK: seeds 1001/1002, single- and multi-wave, G in {1,8}."""
+    M, N, K = shape
+    inp = make_inputs(oracle, M, N, K, "e4m3", 1001, 1002)
+    ref = reference(oracle, inp)
+    for got in _run(b200, inp, variant, "f32", reps=3, group_m=group_m, stages=stages):
+        r = oracle.check_close(got, ref, 3e-2, 3e-2)
+        assert r.mismatches == 0 and np.isfinite(got).all(), (r.max_abs_err, r.max_rel_err)
+
+
+def test_ref_check_fp8_dynamic_queue(b200, oracle):
+    """gemm_fp8_bn128 CHECK (dynamic tile queue -> CLC): seeds 2001/2002, 2048x2048x256."""
+    inp = make_inputs(oracle, 2048, 2048, 256, "e4m3", 2001, 2002)
+    ref = reference(oracle, inp)
+    for got in _run(b200, inp, "clc", "f32", reps=3, group_m=8):
+        r = oracle.check_close(got, ref, 3e-2, 3e-2)
+        assert r.mismatches == 0, (r.max_abs_err, r.max_rel_err)
+
+
+# ------------------------------------------------------------------- BASELINE configs
+@pytest.mark.parametrize("variant", ALL_VARIANTS)
+def test_config1_fp16_512(b200, oracle, variant):
+    inp = make_inputs(oracle, 512, 512, 512, "f16", 601, 602)
+    ref = reference(oracle, inp)
+    for got in _run(b200, inp, variant, "f16", reps=3):
+        ok, info = compare(got, ref, TOL_16)
+        assert ok, info
+
+
+@pytest.mark.parametrize("variant", ALL_VARIANTS)
+def test_config2_fp16_2048(b200, oracle, variant):
+    inp = make_inputs(oracle, 2048, 2048, 2048, "f16", 603, 604)
+    ref = reference(oracle, inp)
+    (got,) = _run(b200, inp, variant, "f16")
+    ok, info = compare(got, ref, TOL_16)
+    assert ok, info
+
+
+@pytest.mark.parametrize("variant", ["2cta", "persistent"])
+def test_config3_bf16_8192_sampled(b200, oracle, variant):
+    """bf16 8192^3, normal(0,1)*0.1 seeds 605/606; seeded row bands vs the oracle."""
+    inp = make_inputs(oracle, 8192, 8192, 8192, "bf16", 605, 606, dist="normal")
+    (got,) = _run(b200, inp, variant, "bf16")
+    for r0, r1 in sample_bands(8192, seed=3, bands=2, rows=32):
+        ref = reference(oracle, inp, rows=(r0, r1))
+        ok, info = compare(got[r0:r1], ref, TOL_16)
+        assert ok, (r0, info)
+
+
+@pytest.mark.parametrize("variant", ALL_VARIANTS)
+def test_config4_e4m3_2048_scaled(b200, oracle, variant):
+    """e4m3 2048^3, uniform seeds 903/904, per-tensor scale amax/448, bf16 out."""
+    inp = make_inputs(oracle, 2048, 2048, 2048, "e4m3", 903, 904, scaled=True)
+    ref = reference(oracle, inp)
+    (got,) = _run(b200, inp, variant, "bf16")
+    ok, info = compare(got, ref, TOL_E4M3)
+    assert ok, info
+
+
+def test_config4_e4m3_8192_scaled_sampled(b200, oracle):
+    inp = make_inputs(oracle, 8192, 8192, 8192, "e4m3", 905, 906, scaled=True)
+    (got,) = _run(b200, inp, "auto", "bf16")
+    for r0, r1 in sample_bands(8192, seed=4, bands=2, rows=32):
+        ref = reference(oracle, inp, rows=(r0, r1))
+        ok, info = compare(got[r0:r1], ref, TOL_E4M3)
+        assert ok, (r0, info)
+
+
+@pytest.mark.parametrize("M,N,K", [(8192, 8192, 1024), (8192, 8192, 4096), (256, 16384, 8192)])
+@pytest.mark.parametrize("variant", ["clc", "persistent", "2cta"])
+def test_config5_persistent_sweep(b200, oracle, M, N, K, variant):
+    inp = make_inputs(oracle, M, N, K, "e4m3", 907, 908, scaled=True)
+    (got,) = _run(b200, inp, variant, "bf16", group_m=8)
+    for r0, r1 in sample_bands(M, seed=5, bands=1, rows=32):
+        ref = reference(oracle, inp, rows=(r0, r1))
+        ok, info = compare(got[r0:r1], ref, TOL_E4M3)
+        assert ok, (r0, info)
+
+
+# ------------------------------------------------------------------------- edge cases
+@pytest.mark.parametrize("variant", ALL_VARIANTS)
+@pytest.mark.parametrize("dtype,out", [("f16", "f16"), ("bf16", "bf16"), ("e4m3", "bf16"),
+                                       ("bf16", "f32")])
+@pytest.mark.parametrize("M,N,K", [(300, 520, 200), (1, 8, 8), (129, 257, 72), (640, 136, 4104)])
+def test_ragged_shapes(b200, oracle, variant, dtype, out, M, N, K):
+    if dtype == "e4m3" and K % 16:
+        pytest.skip("e4m3 rows need K % 16 == 0 for 16-byte strides")
+    if out == "f16" and N % 8:
+        pytest.skip("16-bit C rows need N % 8 == 0")
+    inp = make_inputs(oracle, M, N, K, dtype, 11, 12, scaled=(dtype == "e4m3"))
+    ref = reference(oracle, inp)
+    (got,) = _run(b200, inp, variant, out)
+    ok, info = compare(got, ref, TOL_E4M3 if dtype == "e4m3" else TOL_16)
+    assert ok, info
+
+
+@pytest.mark.parametrize("variant", ["persistent", "2cta"])
+def test_padded_leading_dims(b200, oracle, variant):
+    M, N, K = 384, 512, 320
+    inp = make_inputs(oracle, M, N, K, "bf16", 21, 22)
+    a, b, _, _ = to_device(inp, torch)
+    ap = torch.zeros((M, K + 64), dtype=a.dtype, device="cuda")[:, :K]
+    bp = torch.zeros((N, K + 32), dtype=b.dtype, device="cuda")[:, :K]
+    ap.copy_(a)
+    bp.copy_(b)
+    cbig = torch.full((M, N + 24), 7.0, dtype=torch.bfloat16, device="cuda")
+    c = cbig[:, :N]
+    b200.gemm(ap, bp, c, variant=variant)
+    torch.cuda.synchronize()
+    ok, info = compare(out_to_f32(c, torch), reference(oracle, inp), TOL_16)
+    assert ok, info
+    # the padding columns of C are untouched
+    assert torch.all(cbig[:, N:] == 7.0)
+
+
+def test_k_zero_gives_zero(b200):
+    a = torch.empty((64, 0), dtype=torch.float16, device="cuda")
+    b = torch.empty((32, 0), dtype=torch.float16, device="cuda")
+    c = torch.full((64, 32), 3.0, dtype=torch.float16, device="cuda")
+    b200.gemm(a, b, c)
+    torch.cuda.synchronize()
+    assert torch.all(c == 0)
+
+
+def test_output_dtypes_agree(b200, oracle):
+    inp = make_inputs(oracle, 256, 512, 512, "f16", 31, 32)
+    outs = {o: _run(b200, inp, "persistent", o)[0] for o in ("f16", "bf16", "f32")}
+    ref = reference(oracle, inp)
+    for o, got in outs.items():
+        ok, info = compare(got, ref, TOL_16)
+        assert ok, (o, info)
+    # fp32 C is within fp32 accumulation-order noise of the oracle
+    assert np.max(np.abs(outs["f32"] - ref)) <= 1e-3 * np.max(np.abs(ref))
+
+
+# --------------------------------------------------------------- failure detection
+def test_bounded_wait_reports_timeout_and_context_survives(b200, oracle):
+    """fault_inject=1: the producer issues no loads, so the MMA warp's bounded wait
+    runs out (10 ms limit), the CTA aborts and the host reads the status word."""
+    inp = make_inputs(oracle, 256, 256, 128, "f16", 41, 42)
+    a, b, _, _ = to_device(inp, torch)
+    c = torch.zeros((256, 256), dtype=torch.float16, device="cuda")
+    b200.status()  # clear
+    for variant in ("1cta", "2cta", "clc"):
+        b200.gemm(a, b, c, variant=variant, fault_inject=1, wait_limit_ns=10_000_000)
+        rc, bits = b200.status()
+        assert rc == b200.ERR_DEVICE_TIMEOUT, (variant, rc, hex(bits))
+        assert bits & 0x80000000
+    # the context is still usable: a normal GEMM after the aborted ones is correct
+    (got,) = _run(b200, inp, "persistent", "f16")
+    ok, info = compare(got, reference(oracle, inp), TOL_16)
+    assert ok, info
+
+
+# ------------------------------------------------------------------------ quantiser
+@pytest.mark.parametrize("n", [1, 7, 4096, 1 << 22, (1 << 20) + 3])
+def test_quantizer_matches_oracle(b200, oracle, n):
+    x = oracle.uniform(903, n) * np.float32(3.5)
+    xd = torch.from_numpy(x).cuda()
+    q, s = b200.quantize_e4m3(xd)
+    torch.cuda.synchronize()
+    q_ref, s_ref = oracle.quantize_e4m3_scaled(x)
+    assert np.float32(s.item()) == s_ref
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), q_ref)
+
+
+def test_quantizer_zero_input_scale_one(b200):
+    x = torch.zeros(1000, dtype=torch.float32, device="cuda")
+    q, s = b200.quantize_e4m3(x)
+    torch.cuda.synchronize()
+    assert s.item() == 1.0 and torch.all(q.view(torch.uint8) == 0)
+
+
+def test_quantize_then_gemm_pipeline(b200, oracle):
+    """On-device quantiser feeding the fp8 GEMM equals the host quantiser + oracle."""
+    M = N = K = 1024
+    a32 = oracle.uniform(903, M * K)
+    b32 = oracle.uniform(904, N * K)
+    qa, sa = b200.quantize_e4m3(torch.from_numpy(a32).cuda())
+    qb, sb = b200.quantize_e4m3(torch.from_numpy(b32).cuda())
+    c = b200.gemm(qa.view(M, K), qb.view(N, K), scale_a=sa, scale_b=sb, out_dtype="bf16")
+    torch.cuda.synchronize()
+    inp = make_inputs(oracle, M, N, K, "e4m3", 903, 904, scaled=True)
+    ok, info = compare(out_to_f32(c, torch), reference(oracle, inp), TOL_E4M3)
+    assert ok, info
