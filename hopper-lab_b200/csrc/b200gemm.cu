@@ -204,14 +204,15 @@ static int validate(const B200GemmArgs* a) {
   if (a->M > lim || a->N > lim || a->K > lim) return B200_ERR_SHAPE;
   if (a->group_m < 0 || a->stages < 0) return B200_ERR_INVALID_ARG;
   if (a->M == 0 || a->N == 0) return B200_OK;
-  if (a->lda < a->K || a->ldb < a->K || a->ldc < a->N) return B200_ERR_SHAPE;
-  if (a->lda < 1 || a->ldb < 1) return B200_ERR_SHAPE;
+  if (a->ldc < a->N) return B200_ERR_SHAPE;
   if (!a->C) return B200_ERR_INVALID_ARG;
-  if (a->K > 0 && (!a->A || !a->B)) return B200_ERR_INVALID_ARG;
   const int eb = elem_bytes(a->ab_dtype), ec = elem_bytes(a->c_dtype);
-  if (!aligned16(a->C) || (a->K > 0 && (!aligned16(a->A) || !aligned16(a->B))))
-    return B200_ERR_ALIGN;
-  if ((a->lda * eb) % 16 || (a->ldb * eb) % 16 || (a->ldc * ec) % 16) return B200_ERR_ALIGN;
+  if (!aligned16(a->C) || (a->ldc * ec) % 16) return B200_ERR_ALIGN;
+  if (a->K == 0) return B200_OK;  // A and B are not read: C = 0
+  if (a->lda < a->K || a->ldb < a->K) return B200_ERR_SHAPE;
+  if (!a->A || !a->B) return B200_ERR_INVALID_ARG;
+  if (!aligned16(a->A) || !aligned16(a->B)) return B200_ERR_ALIGN;
+  if ((a->lda * eb) % 16 || (a->ldb * eb) % 16) return B200_ERR_ALIGN;
   // TMA global strides must stay below 2^40 bytes.
   if (a->lda * eb >= (int64_t(1) << 40) || a->ldb * eb >= (int64_t(1) << 40) ||
       a->ldc * ec >= (int64_t(1) << 40))
