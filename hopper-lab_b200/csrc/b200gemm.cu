@@ -14,7 +14,7 @@
 #include <cstring>
 #include <mutex>
 
-#include "../../include/b200gemm.h"
+#include "b200gemm.h"
 #include "gemm_launch.cuh"
 
 namespace {
@@ -105,7 +105,7 @@ int encode_2d(CUtensorMap* m, const void* ptr, int dt, uint64_t rows, uint64_t c
   std::memset(m, 0, sizeof(*m));
   CUresult r = g_encode(m, t, 2, const_cast<void*>(ptr), gdim, gstride, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TMAP;
 }
 
@@ -134,6 +134,11 @@ int variant_shape(int variant, int ab, VariantShape* vs) {
       vs->cg = 2;
       vs->sched = b200::SCHED_STATIC;
       vs->max_stages = GemmCfg<b200::DT_F16, b200::DT_F16, 2, 0>::MAX_STAGES;
+      break;
+    case B200_VARIANT_2CTA_CLC:
+      vs->cg = 2;
+      vs->sched = b200::SCHED_CLC;
+      vs->max_stages = GemmCfg<b200::DT_F16, b200::DT_F16, 2, 1>::MAX_STAGES;
       break;
     default: return B200_ERR_INVALID_ARG;
   }
@@ -197,7 +202,7 @@ static int validate(const B200GemmArgs* a) {
     return B200_ERR_INVALID_ARG;
   if (a->c_dtype != B200_DT_F16 && a->c_dtype != B200_DT_BF16 && a->c_dtype != B200_DT_F32)
     return B200_ERR_INVALID_ARG;
-  if (a->variant < B200_VARIANT_AUTO || a->variant > B200_VARIANT_CLC) return B200_ERR_INVALID_ARG;
+  if (a->variant < B200_VARIANT_AUTO || a->variant > B200_VARIANT_2CTA_CLC) return B200_ERR_INVALID_ARG;
   if (a->M < 0 || a->N < 0 || a->K < 0) return B200_ERR_SHAPE;
   // TMA coordinates are int32 and the tile counters are uint32.
   const int64_t lim = (int64_t(1) << 31) - 1;
@@ -299,6 +304,7 @@ int b200_gemm(const B200GemmArgs* args, void* stream_v) {
       grid = 2u * (kp.num_tiles < pairs ? kp.num_tiles : pairs);
       break;
     }
+    case B200_VARIANT_2CTA_CLC: grid = 2u * kp.num_tiles; break;
     default: return B200_ERR_INVALID_ARG;
   }
 

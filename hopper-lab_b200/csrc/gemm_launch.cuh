@@ -69,6 +69,10 @@ cudaError_t launch_e4m3(int cd, int cg, int sched, const LaunchPlan& lp);
       if (cd == DT_F16) return launch_gemm<AB, DT_F16, 2, SCHED_STATIC>(lp);             \
       if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, 2, SCHED_STATIC>(lp);           \
       if (cd == DT_F32) return launch_gemm<AB, DT_F32, 2, SCHED_STATIC>(lp);             \
+    } else if (cg == 2 && sched == SCHED_CLC) {                                          \
+      if (cd == DT_F16) return launch_gemm<AB, DT_F16, 2, SCHED_CLC>(lp);                \
+      if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, 2, SCHED_CLC>(lp);              \
+      if (cd == DT_F32) return launch_gemm<AB, DT_F32, 2, SCHED_CLC>(lp);                \
     }                                                                                    \
     return cudaErrorNotSupported;                                                        \
   }

@@ -9,8 +9,9 @@
 //
 // What each reference kernel becomes here:
 //   gemm_ws_kernel   (src/05_gemm/gemm_ws.cu:56)   -> CG=1, one tile per CTA
-//   gemm_ws_cluster  (src/06_cluster/gemm_ws_cluster.cu:50) -> CG=2, the CTA pair
-//                    shares B through cta_group::2 (each CTA loads half of it)
+//   gemm_ws_cluster  (src/06_cluster/gemm_ws_cluster.cu:50) -> CG=2: the CTA pair
+//                    runs one cta_group::2 MMA (M=256) and each CTA loads half of
+//                    B, so the pair shares B without any multicast load
 //   gemm_fp8_kernel  (src/07_fp8/gemm_fp8.cu:48)   -> AB = e4m3, kind::f8f6f4,
 //                    per-tensor fp32 scales fused in the epilogue
 //   gemm_fp8_persist (src/08_persistent/gemm_fp8_persist.cu:68) -> SCHED_STATIC
@@ -22,7 +23,7 @@
 // CTA = 256 threads, 8 warps:
 //   warp 0      TMA producer (one lane): A/B k-blocks into an S-stage smem ring
 //   warp 1      TMEM owner + MMA issuer (one lane of the leader CTA)
-//   warp 2      CLC scheduler (one lane; SCHED_CLC only)
+//   warp 2      CLC scheduler (one lane of the leader CTA; SCHED_CLC only)
 //   warp 3      idle
 //   warps 4-7   epilogue: TMEM -> registers -> (scale, narrow) -> swizzled smem ->
 //               TMA store; warp 4+q drains TMEM lanes 32q..32q+31
@@ -104,15 +105,15 @@ struct GemmCfg {
   static constexpr uint32_t ALIGN_SLACK = 1024;
   static constexpr uint32_t MAX_STAGES =
       (MAX_SMEM - EPI_BYTES - BAR_BYTES - ALIGN_SLACK) / STAGE;
-  static constexpr uint32_t DEFAULT_STAGES = MAX_STAGES;
   static constexpr uint32_t NUM_THREADS = 256;
-  static constexpr uint32_t SCHED_CONSUMERS = 6;       // producer + MMA + 4 epilogue warps
+  // CLC ring consumers per CTA: producer + MMA + 4 epilogue warps
+  static constexpr uint32_t SCHED_CONSUMERS = 6;
 
   static uint32_t smem_bytes(uint32_t stages) {
     return stages * STAGE + EPI_BYTES + BAR_BYTES + ALIGN_SLACK;
   }
   static_assert(TMEM_COLS <= 512, "TMEM has 512 columns");
-  static_assert(!(SCHED == SCHED_CLC && CG == 2), "CLC scheduling is built for 1-CTA tiles");
+  static_assert(MAX_STAGES <= 8, "the barrier block holds 8 ring stages");
 };
 
 template <int AB, int CD, int CG, int SCHED>
@@ -123,6 +124,8 @@ __global__ void __launch_bounds__(256, 1)
   extern __shared__ uint8_t smem_raw[];
 
   // ---- shared-memory carve-up (1024-byte aligned for SWIZZLE_128B) ----
+  // Same offsets in both CTAs of a pair: the MMA reads the peer's operand tiles at
+  // the addresses it names for its own, and commits land on the peer's barriers.
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* base_ptr = smem_raw + (base - raw);
@@ -154,9 +157,12 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (uint32_t a = 0; a < 2; ++a) {
       mbar_init(bar_tfull + 8 * a, 1);
+      // every epilogue warp of the pair hands the accumulator back to the leader
       mbar_init(bar_tempty + 8 * a, 4 * CG);
+      // leader: the try_cancel response (tx); peer: the leader's forwarding arrive
       mbar_init(bar_sfull + 8 * a, 1);
-      mbar_init(bar_sempty + 8 * a, Cfg::SCHED_CONSUMERS);
+      // slot release: every consumer of the pair arrives on the leader's barrier
+      mbar_init(bar_sempty + 8 * a, Cfg::SCHED_CONSUMERS * CG);
     }
     mbar_init(bar_done, 1);
     *abort_flag = 0u;
@@ -181,21 +187,26 @@ __global__ void __launch_bounds__(256, 1)
 
   // ---- tile sequence shared by every role ----
   // SCHED_STATIC: cluster c takes tiles c, c + G, c + 2G, ... (G = clusters in grid)
-  // SCHED_CLC   : tile = blockIdx.x first, then whatever try_cancel returns
+  // SCHED_CLC   : tile = this cluster's own index first, then whatever the
+  //               leader's try_cancel returns (forwarded to the peer)
   const uint32_t first_tile = blockIdx.x / CG;
   const uint32_t tile_stride = gridDim.x / CG;
+  const uint32_t leader_sempty0 = (CG == 2) ? mapa_shared(bar_sempty, 0) : bar_sempty;
 
-  // Reads the next tile from the CLC ring (consumer side). Returns false when the
-  // schedule is exhausted or the CTA aborted.
+  // Consumer side of the CLC ring: wait for slot, decode, release it to the leader.
+  // Returns false when the grid is exhausted (tile unchanged) or on abort.
   uint32_t sched_slot = 0, sched_phase = 0;
-  auto clc_next = [&](uint32_t& tile, bool single_lane) -> bool {
-    bool ok = mbar_wait(bar_sfull + 8 * sched_slot, sched_phase, p.wait_ns, abort_flag);
-    if (!ok) { fail(ST_SCHED); return false; }
+  auto clc_next = [&](uint32_t& tile) -> bool {
+    if (!mbar_wait<CG == 2>(bar_sfull + 8 * sched_slot, sched_phase, p.wait_ns, abort_flag)) {
+      fail(ST_SCHED);
+      return false;
+    }
     uint32_t x = 0;
     const bool got = clc_decode(clc_resp + 16 * sched_slot, x);
-    if (single_lane) mbar_arrive(bar_sempty + 8 * sched_slot);
-    if (++sched_slot == 2) { sched_slot = 0; sched_phase ^= 1; }
-    tile = x;
+    if constexpr (CG == 1) mbar_arrive(bar_sempty + 8 * sched_slot);
+    else mbar_arrive_cluster(leader_sempty0 + 8 * sched_slot);
+    if (++sched_slot == 2) { sched_slot = 0; sched_phase ^= 1u; }
+    if (got) tile = x / CG;
     return got;
   };
 
@@ -226,6 +237,9 @@ __global__ void __launch_bounds__(256, 1)
               tma_load_2d(sA + stage * Cfg::A_STAGE, &tmA, kx, a_row, bar_full + 8 * stage, hint);
               tma_load_2d(sB + stage * Cfg::B_STAGE, &tmB, kx, b_row, bar_full + 8 * stage, hint);
             } else {
+              // Both CTAs' bytes are credited to the leader's full barrier; only the
+              // leader arms it (a peer credit that lands first leaves the tx count
+              // negative but cannot complete the phase without the leader's arrive).
               if (rank == 0) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * Cfg::STAGE);
               const uint32_t lf = leader_full0 + 8 * stage;
               tma_load_2d_pair(sA + stage * Cfg::A_STAGE, &tmA, kx, a_row, lf, hint);
@@ -236,7 +250,7 @@ __global__ void __launch_bounds__(256, 1)
           }
           if (!ok) break;
           if constexpr (SCHED == SCHED_CLC) {
-            more = clc_next(tile, true);
+            more = clc_next(tile);
           } else {
             tile += tile_stride;
             more = tile < p.num_tiles;
@@ -249,12 +263,14 @@ __global__ void __launch_bounds__(256, 1)
         if constexpr (CG == 1) {
           const uint32_t first = issued > S ? issued - S : 0u;
           for (uint32_t i = first; i < issued; ++i) {
-            const uint32_t s = i % S, par = (i / S) & 1u;
-            if (!mbar_wait_bounded(bar_full + 8 * s, par, p.wait_ns)) break;
+            if (!mbar_wait_bounded(bar_full + 8 * (i % S), (i / S) & 1u, p.wait_ns)) break;
           }
         } else {
+          // The pair's full barriers live in the leader; give in-flight copies a
+          // fixed 50 us (a 32 KB TMA completes in a few us) before the cluster exits.
           const uint64_t t0 = globaltimer_ns();
-          while (globaltimer_ns() - t0 < 50000ull) { }
+          while (globaltimer_ns() - t0 < 50000ull) {
+          }
         }
       }
     }
@@ -274,12 +290,13 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::BN;
         for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+          // TMA completion on the mbarrier makes the stage visible to the MMA; no
+          // tcgen05 fence is needed between this wait and the MMAs.
           if (!mbar_wait(bar_full + 8 * stage, phase, p.wait_ns, abort_flag)) {
             fail(ST_MMA_FULL);
             ok = false;
             break;
           }
-          tc_fence_after();
           const uint32_t a0 = sA + stage * Cfg::A_STAGE;
           const uint32_t b0 = sB + stage * Cfg::B_STAGE;
 #pragma unroll
@@ -287,16 +304,17 @@ __global__ void __launch_bounds__(256, 1)
             umma<CG, Cfg::KIND>(d_tmem, sdesc_k_sw128(a0 + 32u * k), sdesc_k_sw128(b0 + 32u * k),
                                 Cfg::IDESC, (kb | k) != 0u ? 1u : 0u);
           }
-          umma_commit<CG>(bar_empty + 8 * stage);
-          if constexpr (CG == 2) umma_commit<CG>(mapa_shared(bar_empty + 8 * stage, 1));
+          // frees this stage in both CTAs once the MMAs above have read it
+          if constexpr (CG == 1) umma_commit<1>(bar_empty + 8 * stage);
+          else umma_commit_pair(bar_empty + 8 * stage, 0x3);
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        umma_commit<CG>(bar_tfull + 8 * acc);
-        if constexpr (CG == 2) umma_commit<CG>(mapa_shared(bar_tfull + 8 * acc, 1));
+        if constexpr (CG == 1) umma_commit<1>(bar_tfull + 8 * acc);
+        else umma_commit_pair(bar_tfull + 8 * acc, 0x3);
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         if constexpr (SCHED == SCHED_CLC) {
-          more = clc_next(tile, true);
+          more = clc_next(tile);
         } else {
           tile += tile_stride;
           more = tile < p.num_tiles;
@@ -305,13 +323,20 @@ __global__ void __launch_bounds__(256, 1)
       // Every MMA this thread issued must retire before TMEM is released.
       umma_commit<CG>(bar_done);
       if (!mbar_wait_bounded(bar_done, 0, p.wait_ns)) fail(ST_DRAIN);
+    } else if (SCHED == SCHED_CLC && lane == 0 && rank != 0) {
+      // the peer's MMA warp has no MMA work but still consumes the schedule
+      uint32_t tile = first_tile;
+      bool more = tile < p.num_tiles;
+      while (more) more = clc_next(tile);
     }
     __syncwarp();
   } else if (warp == 2) {
     // ============================== CLC scheduler ==============================
     if constexpr (SCHED == SCHED_CLC) {
-      if (lane == 0 && first_tile < p.num_tiles) {
+      if (lane == 0 && rank == 0 && first_tile < p.num_tiles) {
         uint32_t slot = 0, ph = 0;
+        const uint32_t peer_sfull0 = (CG == 2) ? mapa_shared(bar_sfull, 1) : 0u;
+        const uint32_t peer_resp0 = (CG == 2) ? mapa_shared(clc_resp, 1) : 0u;
         while (true) {
           if (!mbar_wait(bar_sempty + 8 * slot, ph ^ 1u, p.wait_ns, abort_flag)) {
             fail(ST_SCHED);
@@ -324,7 +349,15 @@ __global__ void __launch_bounds__(256, 1)
             break;
           }
           uint32_t x;
-          if (!clc_decode(clc_resp + 16 * slot, x)) break;  // grid exhausted: stop asking
+          const bool got = clc_decode(clc_resp + 16 * slot, x);
+          if constexpr (CG == 2) {
+            // forward the 16-byte response to the peer, then release it there
+            uint32_t r0, r1, r2, r3;
+            ld_shared_v4(clc_resp + 16 * slot, r0, r1, r2, r3);
+            st_shared_cluster_v4(peer_resp0 + 16 * slot, r0, r1, r2, r3);
+            mbar_arrive_cluster(peer_sfull0 + 8 * slot);
+          }
+          if (!got) break;  // grid exhausted: a failed request ends the schedule
           if (++slot == 2) { slot = 0; ph ^= 1u; }
         }
       }
@@ -345,7 +378,17 @@ __global__ void __launch_bounds__(256, 1)
       uint32_t bm, bn;
       tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
       uint32_t okw = 0;
-      if (lane == 0) okw = mbar_wait(bar_tfull + 8 * acc, acc_phase, p.wait_ns, abort_flag) ? 1u : 0u;
+      if (lane == 0) {
+        // The accumulator takes a whole main loop to fill: sleep between polls
+        // (bounded by the same deadline and abort flag as every other wait).
+        const uint64_t t0 = globaltimer_ns();
+        bool done;
+        while (!(done = mbar_try_wait(bar_tfull + 8 * acc, acc_phase))) {
+          if (*abort_flag || globaltimer_ns() - t0 > p.wait_ns) break;
+          __nanosleep(1000);
+        }
+        okw = done ? 1u : 0u;
+      }
       okw = __shfl_sync(0xffffffffu, okw, 0);
       if (!okw) {
         if (lane == 0) fail(ST_EPI_TMEM_FULL);
@@ -415,12 +458,11 @@ __global__ void __launch_bounds__(256, 1)
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
       if constexpr (SCHED == SCHED_CLC) {
-        uint32_t nt = 0;
+        uint32_t nt = tile;
         bool got = false;
-        if (lane == 0) got = clc_next(nt, true);
-        got = __shfl_sync(0xffffffffu, got ? 1u : 0u, 0) != 0u;
+        if (lane == 0) got = clc_next(nt);
+        more = __shfl_sync(0xffffffffu, got ? 1u : 0u, 0) != 0u;
         tile = __shfl_sync(0xffffffffu, nt, 0);
-        more = got;
       } else {
         tile += tile_stride;
         more = tile < p.num_tiles;

@@ -15,7 +15,7 @@
 
 #include <cstdint>
 
-#include "../../include/b200gemm.h"
+#include "b200gemm.h"
 
 namespace {
 

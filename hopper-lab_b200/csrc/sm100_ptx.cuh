@@ -12,8 +12,10 @@
 //   * every mbarrier wait is bounded by %globaltimer and by a CTA-wide abort flag,
 //     so a protocol error becomes an error code instead of a hung GPU
 //     (the reference spins forever: mbarrier.cuh:37-47);
-//   * no TMA load carries .multicast::cluster anywhere in this library, so the same
-//     binary can run on every GPU of a box.
+//   * every TMA load here is a plain unicast copy into the issuing CTA's own shared
+//     memory, so the same binary can run on every GPU of a box; the one cluster-wide
+//     signal is the pair kernel's tcgen05.commit (umma_commit_pair), which moves no
+//     data.
 #pragma once
 
 #include <cuda.h>
@@ -76,19 +78,51 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with a suspend-time hint: a waiting thread is parked by the hardware
+// until the phase completes or about `ns` nanoseconds pass, instead of spinning
+// and taking issue slots from the producer and MMA warps.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return done != 0;
+}
+
+// Same, with acquire semantics at cluster scope: for barriers that another CTA of
+// the cluster completes with a release.cluster arrive after writing our smem.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return done != 0;
+}
+
+constexpr uint32_t kSuspendHintNs = 100000u;  // re-check abort / deadline every ~100 us
+
 // Bounded wait. Returns true when the phase with `parity` completed; false when
 // either `limit_ns` of %globaltimer elapsed or another role of the CTA raised
 // `*abort`. The caller turns `false` into an error code and leaves its loop.
+template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns,
                                           volatile uint32_t* abort) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (kClusterScope ? mbar_try_wait_cluster(bar, parity, 0u) : mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 63u) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > limit_ns) return false;
-    }
+  for (;;) {
+    if (kClusterScope ? mbar_try_wait_cluster(bar, parity, kSuspendHintNs)
+                      : mbar_try_wait_hint(bar, parity, kSuspendHintNs))
+      return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -97,9 +131,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 63u && globaltimer_ns() - t0 > limit_ns) return false;
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, kSuspendHintNs)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -125,12 +159,21 @@ __device__ __forceinline__ void cluster_sync() {
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+__device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b,
+                                                     uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c,
+                                             uint32_t& d) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(addr)
+               : "memory");
 }
 
 // ---------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), never with multicast
+// TMA (cp.async.bulk.tensor): unicast loads and stores only
 // ---------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
@@ -303,9 +346,9 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t b
   }
 }
 
-// Arrive once on `bar` (a shared::cluster address; a local shared::cta address is
-// valid too) when every tcgen05 async operation issued so far by this thread has
-// completed. No multicast form is used: a pair kernel commits once per CTA.
+// Arrive once on `bar` when every tcgen05 async operation issued so far by this
+// thread has completed. `bar` is a shared::cluster address (a local shared::cta
+// address is valid too).
 template <int CG>
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   if constexpr (CG == 1)
@@ -314,6 +357,17 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
   else
     asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
+}
+
+// Pair form: one commit that arrives on the barrier at the same shared-memory
+// offset in every CTA of `cta_mask` (bit r = cluster rank r): a completion signal
+// inside this GPU's own CTA pair. It moves no data.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          bar),
+      "h"(cta_mask)
+      : "memory");
 }
 
 // ---------------------------------------------------------------------------------

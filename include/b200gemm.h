@@ -49,8 +49,10 @@ enum {
                                   static schedule            (06_cluster gemm_ws_cluster)*/
   B200_VARIANT_PERSISTENT = 3, /* 1-CTA, grid = SM count, static group-M schedule
                                                               (08_persistent persist)  */
-  B200_VARIANT_CLC = 4         /* 1-CTA, cluster-launch-control work stealing
+  B200_VARIANT_CLC = 4,        /* 1-CTA, cluster-launch-control work stealing
                                                               (08_persistent bn128 dyn)*/
+  B200_VARIANT_2CTA_CLC = 5    /* cta_group::2 pair + cluster-launch-control work
+                                  stealing (the pair form of the persistent kernel) */
 };
 
 /* return codes */

@@ -79,8 +79,9 @@ def test_variant_info(b200):
         info = b200.variant_info(v)
         assert info["tile_m"] == 128 and info["tile_n"] == 256
         assert info["max_stages"] == 4
-    info = b200.variant_info("2cta", b200.DT_E4M3)
-    assert info["tile_m"] == 256 and info["tile_n"] == 256 and info["max_stages"] == 6
+    for v in ("2cta", "2cta_clc"):
+        info = b200.variant_info(v, b200.DT_E4M3)
+        assert info["tile_m"] == 256 and info["tile_n"] == 256 and info["max_stages"] == 6
     with pytest.raises(b200.B200Error):
         b200.variant_info(0)  # AUTO has no fixed shape
     with pytest.raises(b200.B200Error):
@@ -153,7 +154,9 @@ def test_python_wrapper_checks_shapes(b200):
 def test_product_path_has_no_oracle_or_fallback():
     """The library and its Python mirror never reach into oracle/ or a CPU GEMM."""
     pkg = ROOT / "hopper-lab_b200"
-    for f in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cuh")):
+    product = [f for f in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cuh"))
+               if f.name != "profile_case.py"]  # the profiling driver times cuBLAS on purpose
+    for f in product:
         text = f.read_text()
         assert "import oracle" not in text and "oracle/" not in text.replace("oracle/_ref", ""), f
         assert "torch.matmul" not in text, f

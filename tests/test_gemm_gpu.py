@@ -23,7 +23,7 @@ from gemm_check import (TOL_16, TOL_E4M3, compare, make_inputs, out_to_f32, refe
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-ALL_VARIANTS = ["1cta", "persistent", "clc", "2cta"]
+ALL_VARIANTS = ["1cta", "persistent", "clc", "2cta", "2cta_clc"]
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -74,7 +74,7 @@ def test_ref_check_fp8_512(b200, oracle, variant):
 @pytest.mark.parametrize("shape", [(512, 512, 256), (2048, 2048, 256)])
 @pytest.mark.parametrize("group_m", [1, 8])
 @pytest.mark.parametrize("variant,stages", [("persistent", 2), ("persistent", 4), ("clc", 4),
-                                            ("2cta", 6)])
+                                            ("2cta", 6), ("2cta_clc", 3)])
 def test_ref_check_fp8_persistent(b200, oracle, shape, group_m, variant, stages):
     """gemm_fp8_persist CHECK: seeds 1001/1002, single- and multi-wave, G in {1,8}."""
     M, N, K = shape
@@ -85,11 +85,12 @@ def test_ref_check_fp8_persistent(b200, oracle, shape, group_m, variant, stages)
         assert r.mismatches == 0 and np.isfinite(got).all(), (r.max_abs_err, r.max_rel_err)
 
 
-def test_ref_check_fp8_dynamic_queue(b200, oracle):
+@pytest.mark.parametrize("variant", ["clc", "2cta_clc"])
+def test_ref_check_fp8_dynamic_queue(b200, oracle, variant):
     """gemm_fp8_bn128 CHECK (dynamic tile queue -> CLC): seeds 2001/2002, 2048x2048x256."""
     inp = make_inputs(oracle, 2048, 2048, 256, "e4m3", 2001, 2002)
     ref = reference(oracle, inp)
-    for got in _run(b200, inp, "clc", "f32", reps=3, group_m=8):
+    for got in _run(b200, inp, variant, "f32", reps=3, group_m=8):
         r = oracle.check_close(got, ref, 3e-2, 3e-2)
         assert r.mismatches == 0, (r.max_abs_err, r.max_rel_err)
 
@@ -144,7 +145,7 @@ def test_config4_e4m3_8192_scaled_sampled(b200, oracle):
 
 
 @pytest.mark.parametrize("M,N,K", [(8192, 8192, 1024), (8192, 8192, 4096), (256, 16384, 8192)])
-@pytest.mark.parametrize("variant", ["clc", "persistent", "2cta"])
+@pytest.mark.parametrize("variant", ["clc", "persistent", "2cta", "2cta_clc"])
 def test_config5_persistent_sweep(b200, oracle, M, N, K, variant):
     inp = make_inputs(oracle, M, N, K, "e4m3", 907, 908, scaled=True)
     (got,) = _run(b200, inp, variant, "bf16", group_m=8)
@@ -221,7 +222,7 @@ def test_bounded_wait_reports_timeout_and_context_survives(b200, oracle):
     a, b, _, _ = to_device(inp, torch)
     c = torch.zeros((256, 256), dtype=torch.float16, device="cuda")
     b200.status()  # clear
-    for variant in ("1cta", "2cta", "clc"):
+    for variant in ("1cta", "2cta", "clc", "2cta_clc"):
         b200.gemm(a, b, c, variant=variant, fault_inject=1, wait_limit_ns=10_000_000)
         rc, bits = b200.status()
         assert rc == b200.ERR_DEVICE_TIMEOUT, (variant, rc, hex(bits))
