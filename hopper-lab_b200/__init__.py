@@ -69,6 +69,8 @@ class GemmArgs(C.Structure):
         ("stages", C.c_int32),
         ("fault_inject", C.c_int32),
         ("wait_limit_ns", C.c_uint64),
+        ("tile_n", C.c_int32),
+        ("reserved", C.c_int32),
     ]
 
 
@@ -116,9 +118,10 @@ def strerror(code: int) -> str:
         return f"error {code}"
 
 
-def variant_info(variant: str | int, ab_dtype: int = DT_F16):
+def variant_info(variant: str | int, ab_dtype: int = DT_F16, tile_n: int = 0):
     v = VARIANTS[variant] if isinstance(variant, str) else int(variant)
     out = [C.c_int32() for _ in range(4)]
+    out[1].value = tile_n
     rc = lib().b200_gemm_variant_info(v, ab_dtype, *[C.byref(o) for o in out])
     if rc != OK:
         raise B200Error(rc, "variant_info")
@@ -170,7 +173,7 @@ def _stream_handle(stream) -> int:
 
 
 def make_args(a, b, c, *, scale_a=None, scale_b=None, variant="auto", group_m=0, stages=0,
-              wait_limit_ns=0, fault_inject=0) -> GemmArgs:
+              wait_limit_ns=0, fault_inject=0, tile_n=0) -> GemmArgs:
     """Fill B200GemmArgs from 2-D torch tensors (row-major, unit column stride)."""
     for name, t in (("A", a), ("B", b), ("C", c)):
         if t.dim() != 2 or (t.numel() > 0 and t.stride(1) != 1):
@@ -196,12 +199,13 @@ def make_args(a, b, c, *, scale_a=None, scale_b=None, variant="auto", group_m=0,
     args.stages = stages
     args.fault_inject = fault_inject
     args.wait_limit_ns = wait_limit_ns
+    args.tile_n = tile_n
     return args
 
 
 def gemm(a, b, c=None, *, out_dtype="bf16", scale_a=None, scale_b=None, variant="auto",
          group_m: int = 0, stages: int = 0, wait_limit_ns: int = 0, fault_inject: int = 0,
-         stream=None):
+         tile_n: int = 0, stream=None):
     """C = scale_a * scale_b * A . B^T on the GPU (A: M x K, B: N x K, both row-major).
 
     A/B: torch.float16 | torch.bfloat16 | torch.float8_e4m3fn (or uint8 bits).
@@ -213,7 +217,8 @@ def gemm(a, b, c=None, *, out_dtype="bf16", scale_a=None, scale_b=None, variant=
         c = torch.empty((a.shape[0], b.shape[0]), dtype=_torch_dtype(_dtype_code(out_dtype)),
                         device=a.device)
     args = make_args(a, b, c, scale_a=scale_a, scale_b=scale_b, variant=variant, group_m=group_m,
-                     stages=stages, wait_limit_ns=wait_limit_ns, fault_inject=fault_inject)
+                     stages=stages, wait_limit_ns=wait_limit_ns, fault_inject=fault_inject,
+                     tile_n=tile_n)
     rc = lib().b200_gemm(C.byref(args), C.c_void_p(_stream_handle(stream)))
     if rc != OK:
         raise B200Error(rc, "b200_gemm")

@@ -110,44 +110,62 @@ int encode_2d(CUtensorMap* m, const void* ptr, int dt, uint64_t rows, uint64_t c
 }
 
 struct VariantShape {
-  int cg, sched;
-  uint32_t tile_m, tile_n, max_stages, default_stages;
+  int cg, sched, nh;
+  uint32_t tile_m, tile_n, max_stages, default_stages, atoms, smem_per_stage_cfg;
 };
 
-// Tile facts per variant; every variant uses BN = 256 and BM = 128 per CTA.
-int variant_shape(int variant, int ab, VariantShape* vs) {
-  const bool fp8 = (ab == B200_DT_E4M3);
-  (void)fp8;
+// Tile and ring facts of one kernel configuration. Stage bytes do not depend on
+// the element type (one 128-byte K atom per row), so the f16 instantiation's
+// constants stand for every dtype.
+template <int CG, int SCHED, int NH>
+void fill_shape(VariantShape* vs) {
+  using Cfg = GemmCfg<b200::DT_F16, b200::DT_F16, CG, SCHED, NH>;
+  vs->cg = CG;
+  vs->sched = SCHED;
+  vs->nh = NH;
+  vs->tile_m = uint32_t(Cfg::BM * CG);
+  vs->tile_n = uint32_t(Cfg::BN);
+  vs->max_stages = Cfg::MAX_STAGES;
+  vs->default_stages = Cfg::MAX_STAGES;
+  vs->atoms = uint32_t(Cfg::ATOMS);
+}
+
+template <int CG, int SCHED, int NH>
+uint32_t shape_smem(uint32_t stages) {
+  return GemmCfg<b200::DT_F16, b200::DT_F16, CG, SCHED, NH>::smem_bytes(stages);
+}
+
+// `tile_n` 0 picks the variant's default width (256).
+int variant_shape(int variant, int tile_n, VariantShape* vs) {
+  if (tile_n != 0 && tile_n != 256 && tile_n != 512) return B200_ERR_INVALID_ARG;
+  const bool wide = (tile_n == 512);
   switch (variant) {
     case B200_VARIANT_1CTA:
     case B200_VARIANT_PERSISTENT:
-      vs->cg = 1;
-      vs->sched = b200::SCHED_STATIC;
-      vs->max_stages = GemmCfg<b200::DT_F16, b200::DT_F16, 1, 0>::MAX_STAGES;
+      if (wide) return B200_ERR_INVALID_ARG;
+      fill_shape<1, b200::SCHED_STATIC, 1>(vs);
       break;
     case B200_VARIANT_CLC:
-      vs->cg = 1;
-      vs->sched = b200::SCHED_CLC;
-      vs->max_stages = GemmCfg<b200::DT_F16, b200::DT_F16, 1, 1>::MAX_STAGES;
+      if (wide) return B200_ERR_INVALID_ARG;
+      fill_shape<1, b200::SCHED_CLC, 1>(vs);
       break;
     case B200_VARIANT_2CTA:
-      vs->cg = 2;
-      vs->sched = b200::SCHED_STATIC;
-      vs->max_stages = GemmCfg<b200::DT_F16, b200::DT_F16, 2, 0>::MAX_STAGES;
+      if (wide) fill_shape<2, b200::SCHED_STATIC, 2>(vs);
+      else fill_shape<2, b200::SCHED_STATIC, 1>(vs);
       break;
     case B200_VARIANT_2CTA_CLC:
-      vs->cg = 2;
-      vs->sched = b200::SCHED_CLC;
-      vs->max_stages = GemmCfg<b200::DT_F16, b200::DT_F16, 2, 1>::MAX_STAGES;
+      if (wide) fill_shape<2, b200::SCHED_CLC, 2>(vs);
+      else fill_shape<2, b200::SCHED_CLC, 1>(vs);
       break;
     default: return B200_ERR_INVALID_ARG;
   }
-  // Stage bytes do not depend on the element type (one 128-byte K atom per row).
-  if (vs->max_stages > 8) vs->max_stages = 8;
-  vs->default_stages = vs->max_stages;
-  vs->tile_m = 128u * vs->cg;
-  vs->tile_n = 256u;
   return B200_OK;
+}
+
+uint32_t variant_smem(const VariantShape& vs, uint32_t stages) {
+  if (vs.cg == 1) return shape_smem<1, 0, 1>(stages);
+  if (vs.nh == 1) return shape_smem<2, 0, 1>(stages);
+  return shape_smem<2, 0, 2>(stages);
 }
 
 int pick_variant(const B200GemmArgs* a, int sms) {
@@ -186,7 +204,7 @@ int b200_gemm_variant_info(int32_t variant, int32_t ab_dtype, int32_t* tile_m, i
   if (ab_dtype != B200_DT_F16 && ab_dtype != B200_DT_BF16 && ab_dtype != B200_DT_E4M3)
     return B200_ERR_INVALID_ARG;
   VariantShape vs;
-  int rc = variant_shape(variant, ab_dtype, &vs);
+  int rc = variant_shape(variant, tile_n ? *tile_n : 0, &vs);
   if (rc != B200_OK) return rc;
   if (tile_m) *tile_m = static_cast<int32_t>(vs.tile_m);
   if (tile_n) *tile_n = static_cast<int32_t>(vs.tile_n);
@@ -207,7 +225,8 @@ static int validate(const B200GemmArgs* a) {
   // TMA coordinates are int32 and the tile counters are uint32.
   const int64_t lim = (int64_t(1) << 31) - 1;
   if (a->M > lim || a->N > lim || a->K > lim) return B200_ERR_SHAPE;
-  if (a->group_m < 0 || a->stages < 0) return B200_ERR_INVALID_ARG;
+  if (a->group_m < 0 || a->stages < 0 || a->reserved != 0) return B200_ERR_INVALID_ARG;
+  if (a->tile_n != 0 && a->tile_n != 256 && a->tile_n != 512) return B200_ERR_INVALID_ARG;
   if (a->M == 0 || a->N == 0) return B200_OK;
   if (a->ldc < a->N) return B200_ERR_SHAPE;
   if (!a->C) return B200_ERR_INVALID_ARG;
@@ -257,19 +276,21 @@ int b200_gemm(const B200GemmArgs* args, void* stream_v) {
 
   const int variant = (a.variant == B200_VARIANT_AUTO) ? pick_variant(&a, g_sm_count[dev]) : a.variant;
   VariantShape vs;
-  rc = variant_shape(variant, a.ab_dtype, &vs);
+  rc = variant_shape(variant, a.tile_n, &vs);
   if (rc != B200_OK) return rc;
   const uint32_t stages = a.stages ? uint32_t(a.stages) : vs.default_stages;
   if (stages < 2 || stages > vs.max_stages) return B200_ERR_INVALID_ARG;
 
+  // K per TMA box (one 128-byte atom) and per pipeline stage (atoms x box)
   const uint32_t bk = (a.ab_dtype == B200_DT_E4M3) ? 128u : 64u;
+  const uint32_t stage_k = bk * vs.atoms;
   const uint32_t cd_cols = 128u / uint32_t(ec);
 
   alignas(64) CUtensorMap tA, tB, tC;
   rc = encode_2d(&tA, a.A, a.ab_dtype, uint64_t(a.M), uint64_t(a.K), uint64_t(a.lda), 128u, bk);
   if (rc != B200_OK) return rc;
   rc = encode_2d(&tB, a.B, a.ab_dtype, uint64_t(a.N), uint64_t(a.K), uint64_t(a.ldb),
-                 vs.tile_n / uint32_t(vs.cg), bk);
+                 256u / uint32_t(vs.cg), bk);
   if (rc != B200_OK) return rc;
   rc = encode_2d(&tC, a.C, a.c_dtype, uint64_t(a.M), uint64_t(a.N), uint64_t(a.ldc), 32u, cd_cols);
   if (rc != B200_OK) return rc;
@@ -284,7 +305,7 @@ int b200_gemm(const B200GemmArgs* args, void* stream_v) {
   const uint64_t tiles = uint64_t(kp.m_tiles) * kp.n_tiles;
   if (tiles > 0x7fffffffull / 2) return B200_ERR_SHAPE;
   kp.num_tiles = uint32_t(tiles);
-  kp.k_blocks = uint32_t((a.K + bk - 1) / bk);
+  kp.k_blocks = uint32_t((a.K + stage_k - 1) / stage_k);
   kp.stages = stages;
   kp.group_m = a.group_m ? uint32_t(a.group_m) : uint32_t(kDefaultGroupM);
   kp.fault_inject = a.fault_inject ? 1u : 0u;
@@ -316,14 +337,13 @@ int b200_gemm(const B200GemmArgs* args, void* stream_v) {
   lp.grid = grid;
   lp.stream = stream;
   // smem_bytes() depends only on the stage size, identical for every dtype.
-  lp.smem = (vs.cg == 1) ? GemmCfg<b200::DT_F16, b200::DT_F16, 1, 0>::smem_bytes(stages)
-                         : GemmCfg<b200::DT_F16, b200::DT_F16, 2, 0>::smem_bytes(stages);
+  lp.smem = variant_smem(vs, stages);
 
   cudaError_t e;
   switch (a.ab_dtype) {
-    case B200_DT_F16: e = b200::launch_f16(a.c_dtype, vs.cg, vs.sched, lp); break;
-    case B200_DT_BF16: e = b200::launch_bf16(a.c_dtype, vs.cg, vs.sched, lp); break;
-    default: e = b200::launch_e4m3(a.c_dtype, vs.cg, vs.sched, lp); break;
+    case B200_DT_F16: e = b200::launch_f16(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
+    case B200_DT_BF16: e = b200::launch_bf16(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
+    default: e = b200::launch_e4m3(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
   }
   if (e == cudaErrorNotSupported) return B200_ERR_UNSUPPORTED;
   if (e != cudaSuccess) {

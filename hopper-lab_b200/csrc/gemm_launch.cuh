@@ -17,9 +17,10 @@ struct LaunchPlan {
   cudaStream_t stream;
 };
 
-template <int AB, int CD, int CG, int SCHED>
+template <int AB, int CD, int CG, int SCHED, int NH>
 cudaError_t launch_gemm(const LaunchPlan& lp) {
-  auto kern = gemm_tcgen05_kernel<AB, CD, CG, SCHED>;
+  using Cfg = GemmCfg<AB, CD, CG, SCHED, NH>;
+  auto kern = gemm_tcgen05_kernel<AB, CD, CG, SCHED, NH>;
   // The opt-in shared-memory size is a per-function, per-device attribute.
   static int configured[64] = {0};
   int dev = 0;
@@ -28,14 +29,13 @@ cudaError_t launch_gemm(const LaunchPlan& lp) {
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
     e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(GemmCfg<AB, CD, CG, SCHED>::MAX_SMEM));
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Cfg::MAX_SMEM));
     if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(lp.grid, 1, 1);
-  cfg.blockDim = dim3(GemmCfg<AB, CD, CG, SCHED>::NUM_THREADS, 1, 1);
+  cfg.blockDim = dim3(Cfg::NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = lp.smem;
   cfg.stream = lp.stream;
   cudaLaunchAttribute attr[1];
@@ -50,29 +50,30 @@ cudaError_t launch_gemm(const LaunchPlan& lp) {
   return cudaLaunchKernelEx(&cfg, kern, *lp.a, *lp.b, *lp.c, lp.kp);
 }
 
-// One dispatch entry per (AB, CD, variant) — defined in the instantiation units.
-cudaError_t launch_f16(int cd, int cg, int sched, const LaunchPlan& lp);
-cudaError_t launch_bf16(int cd, int cg, int sched, const LaunchPlan& lp);
-cudaError_t launch_e4m3(int cd, int cg, int sched, const LaunchPlan& lp);
+// One dispatch entry per A/B type — defined in the instantiation units. Selects
+// the instantiation for (C type, CTAs per tile, schedule, N-halves per tile).
+cudaError_t launch_f16(int cd, int cg, int sched, int nh, const LaunchPlan& lp);
+cudaError_t launch_bf16(int cd, int cg, int sched, int nh, const LaunchPlan& lp);
+cudaError_t launch_e4m3(int cd, int cg, int sched, int nh, const LaunchPlan& lp);
+
+#define B200_DISPATCH_CD(AB, CG, SCHED, NH)                                              \
+  do {                                                                                   \
+    if (cd == DT_F16) return launch_gemm<AB, DT_F16, CG, SCHED, NH>(lp);                 \
+    if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, CG, SCHED, NH>(lp);               \
+    if (cd == DT_F32) return launch_gemm<AB, DT_F32, CG, SCHED, NH>(lp);                 \
+  } while (0)
 
 #define B200_DEFINE_DISPATCH(NAME, AB)                                                  \
-  cudaError_t NAME(int cd, int cg, int sched, const LaunchPlan& lp) {                   \
-    if (cg == 1 && sched == SCHED_STATIC) {                                              \
-      if (cd == DT_F16) return launch_gemm<AB, DT_F16, 1, SCHED_STATIC>(lp);             \
-      if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, 1, SCHED_STATIC>(lp);           \
-      if (cd == DT_F32) return launch_gemm<AB, DT_F32, 1, SCHED_STATIC>(lp);             \
-    } else if (cg == 1 && sched == SCHED_CLC) {                                          \
-      if (cd == DT_F16) return launch_gemm<AB, DT_F16, 1, SCHED_CLC>(lp);                \
-      if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, 1, SCHED_CLC>(lp);              \
-      if (cd == DT_F32) return launch_gemm<AB, DT_F32, 1, SCHED_CLC>(lp);                \
-    } else if (cg == 2 && sched == SCHED_STATIC) {                                       \
-      if (cd == DT_F16) return launch_gemm<AB, DT_F16, 2, SCHED_STATIC>(lp);             \
-      if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, 2, SCHED_STATIC>(lp);           \
-      if (cd == DT_F32) return launch_gemm<AB, DT_F32, 2, SCHED_STATIC>(lp);             \
-    } else if (cg == 2 && sched == SCHED_CLC) {                                          \
-      if (cd == DT_F16) return launch_gemm<AB, DT_F16, 2, SCHED_CLC>(lp);                \
-      if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, 2, SCHED_CLC>(lp);              \
-      if (cd == DT_F32) return launch_gemm<AB, DT_F32, 2, SCHED_CLC>(lp);                \
+  cudaError_t NAME(int cd, int cg, int sched, int nh, const LaunchPlan& lp) {           \
+    if (cg == 1 && nh == 1) {                                                            \
+      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 1, SCHED_STATIC, 1);               \
+      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 1, SCHED_CLC, 1);                     \
+    } else if (cg == 2 && nh == 1) {                                                     \
+      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 1);               \
+      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 1);                     \
+    } else if (cg == 2 && nh == 2) {                                                     \
+      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 2);               \
+      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 2);                     \
     }                                                                                    \
     return cudaErrorNotSupported;                                                        \
   }

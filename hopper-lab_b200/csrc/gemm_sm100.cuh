@@ -22,13 +22,17 @@
 //
 // CTA = 256 threads, 8 warps:
 //   warp 0      TMA producer (one lane): A/B k-blocks into an S-stage smem ring
+//               (one 128-byte K atom per stage for 1-CTA tiles, two for pairs)
 //   warp 1      TMEM owner + MMA issuer (one lane of the leader CTA)
 //   warp 2      CLC scheduler (one lane of the leader CTA; SCHED_CLC only)
 //   warp 3      idle
 //   warps 4-7   epilogue: TMEM -> registers -> (scale, narrow) -> swizzled smem ->
 //               TMA store; warp 4+q drains TMEM lanes 32q..32q+31
-// Two fp32 accumulators of BN columns each live in TMEM, so the epilogue of tile t
-// overlaps the main loop of tile t+1.
+// TMEM holds two 256-column fp32 slots. A tile of NH = 1 half (BN = 256) uses one
+// slot, so the epilogue of tile t overlaps the main loop of tile t+1. A pair tile of
+// NH = 2 halves (256 x 512, two N=256 MMAs per K-step sharing the A tiles, 25% less
+// operand traffic per flop) uses both slots; the epilogue releases each slot as
+// soon as it is drained, and the next tile's first MMAs into that slot start then.
 #pragma once
 
 #include "sm100_ptx.cuh"
@@ -79,27 +83,37 @@ __host__ __device__ inline void tile_to_bmn(uint32_t tile, uint32_t num_bm, uint
   bn = t / gsize;
 }
 
-template <int AB, int CD, int CG, int SCHED>
+template <int AB, int CD, int CG, int SCHED, int NH>
 struct GemmCfg {
   static constexpr int BM = 128;                       // rows of C per CTA
-  static constexpr int BN = 256;                       // columns of C per tile (MMA N)
+  static constexpr int MMA_N = 256;                    // N of one tcgen05.mma
+  static constexpr int BN = MMA_N * NH;                // columns of C per tile
   static constexpr int KIND = (AB == DT_E4M3) ? 1 : 0; // 0 kind::f16, 1 kind::f8f6f4
   static constexpr int AB_BYTES = (AB == DT_E4M3) ? 1 : 2;
-  static constexpr int BK = 128 / AB_BYTES;            // one 128-byte swizzle atom of K
-  static constexpr int KSTEPS = 4;                     // 32-byte MMA K-steps per k-block
-  static constexpr int B_ROWS = BN / CG;               // rows of B held by each CTA
-  static constexpr uint32_t A_STAGE = BM * 128;        // bytes
-  static constexpr uint32_t B_STAGE = B_ROWS * 128;
+  // One 128-byte swizzle atom of K per TMA box. A pair stage carries two atoms:
+  // one commit / barrier round trip per 8 MMAs instead of 4 keeps the tensor pipe
+  // busy (the per-stage commit costs tensor-pipe time); 1-CTA stages are already
+  // 48 KB and keep one atom so that four of them fit.
+  static constexpr int ATOMS = (CG == 2 && NH == 1) ? 2 : 1;
+  static constexpr int ATOM_K = 128 / AB_BYTES;        // elements of K per atom
+  static constexpr int BK = ATOMS * ATOM_K;            // elements of K per stage
+  static constexpr int KSTEPS = 4 * ATOMS;             // 32-byte MMA K-steps per stage
+  static constexpr int B_HALF_ROWS = MMA_N / CG;       // rows of B per CTA per N-half
+  static constexpr uint32_t B_HALF = B_HALF_ROWS * 128; // bytes of one half in one atom
+  static constexpr uint32_t A_ATOM = BM * 128;         // bytes
+  static constexpr uint32_t B_ATOM = NH * B_HALF;
+  static constexpr uint32_t A_STAGE = ATOMS * A_ATOM;
+  static constexpr uint32_t B_STAGE = ATOMS * B_ATOM;
   static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
   static constexpr int CD_BYTES = (CD == DT_F32) ? 4 : 2;
   static constexpr int EPI_COLS = 128 / CD_BYTES;      // C columns per 128-byte chunk
-  static constexpr int EPI_CHUNKS = BN / EPI_COLS;
+  static constexpr int EPI_CHUNKS = MMA_N / EPI_COLS; // per 256-column slot
   static constexpr uint32_t EPI_BUF = 32 * 128;        // 32 rows × 128 bytes
   static constexpr uint32_t EPI_BYTES = 4 * 2 * EPI_BUF;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;        // two fp32 accumulators
+  static constexpr uint32_t TMEM_COLS = 512;           // two 256-column fp32 slots
   static constexpr uint32_t MMA_M = BM * CG;
   static constexpr uint32_t IDESC =
-      idesc_f32acc(AB == DT_BF16 ? 1u : 0u, AB == DT_BF16 ? 1u : 0u, MMA_M, BN);
+      idesc_f32acc(AB == DT_BF16 ? 1u : 0u, AB == DT_BF16 ? 1u : 0u, MMA_M, MMA_N);
   static constexpr uint32_t MAX_SMEM = 232448;         // 227 KB opt-in per CTA
   static constexpr uint32_t BAR_BYTES = 256;
   static constexpr uint32_t ALIGN_SLACK = 1024;
@@ -112,15 +126,15 @@ struct GemmCfg {
   static uint32_t smem_bytes(uint32_t stages) {
     return stages * STAGE + EPI_BYTES + BAR_BYTES + ALIGN_SLACK;
   }
-  static_assert(TMEM_COLS <= 512, "TMEM has 512 columns");
+  static_assert(NH == 1 || (NH == 2 && CG == 2), "512-wide tiles are built for CTA pairs");
   static_assert(MAX_STAGES <= 8, "the barrier block holds 8 ring stages");
 };
 
-template <int AB, int CD, int CG, int SCHED>
+template <int AB, int CD, int CG, int SCHED, int NH>
 __global__ void __launch_bounds__(256, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const KParams p) {
-  using Cfg = GemmCfg<AB, CD, CG, SCHED>;
+  using Cfg = GemmCfg<AB, CD, CG, SCHED, NH>;
   extern __shared__ uint8_t smem_raw[];
 
   // ---- shared-memory carve-up (1024-byte aligned for SWIZZLE_128B) ----
@@ -185,6 +199,12 @@ __global__ void __launch_bounds__(256, 1)
     if (p.status) atomicOr(p.status, code | ST_ABORTED);
   };
 
+  // ---- TMEM slots: tile `it`, N-half h -> slot; each use of a slot flips its phase ----
+  // NH = 1: tiles alternate between the two slots (double buffering).
+  // NH = 2: every tile uses both slots, half h in slot h.
+  auto acc_slot = [](uint32_t it, int h) -> uint32_t { return NH == 1 ? (it & 1u) : uint32_t(h); };
+  auto acc_use = [](uint32_t it) -> uint32_t { return NH == 1 ? (it >> 1) : it; };
+
   // ---- tile sequence shared by every role ----
   // SCHED_STATIC: cluster c takes tiles c, c + G, c + 2G, ... (G = clusters in grid)
   // SCHED_CLC   : tile = this cluster's own index first, then whatever the
@@ -224,7 +244,8 @@ __global__ void __launch_bounds__(256, 1)
           uint32_t bm, bn;
           tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
           const int32_t a_row = int32_t((bm * CG + rank) * Cfg::BM);
-          const int32_t b_row = int32_t(bn * Cfg::BN + rank * Cfg::B_ROWS);
+          // rows of this CTA's share of N-half h: bn*BN + h*256 + rank*B_HALF_ROWS
+          const int32_t b_row = int32_t(bn * Cfg::BN + rank * Cfg::B_HALF_ROWS);
           for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
             if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, p.wait_ns, abort_flag)) {
               fail(ST_PRODUCER_EMPTY);
@@ -234,16 +255,30 @@ __global__ void __launch_bounds__(256, 1)
             const int32_t kx = int32_t(kb * Cfg::BK);
             if constexpr (CG == 1) {
               mbar_arrive_expect_tx(bar_full + 8 * stage, Cfg::STAGE);
-              tma_load_2d(sA + stage * Cfg::A_STAGE, &tmA, kx, a_row, bar_full + 8 * stage, hint);
-              tma_load_2d(sB + stage * Cfg::B_STAGE, &tmB, kx, b_row, bar_full + 8 * stage, hint);
+#pragma unroll
+              for (int at = 0; at < Cfg::ATOMS; ++at) {
+                const int32_t x = kx + at * Cfg::ATOM_K;
+                tma_load_2d(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM, &tmA, x, a_row, bar_full + 8 * stage, hint);
+#pragma unroll
+                for (int h = 0; h < NH; ++h)
+                  tma_load_2d(sB + stage * Cfg::B_STAGE + at * Cfg::B_ATOM + h * Cfg::B_HALF, &tmB, x,
+                              b_row + h * Cfg::MMA_N, bar_full + 8 * stage, hint);
+              }
             } else {
               // Both CTAs' bytes are credited to the leader's full barrier; only the
               // leader arms it (a peer credit that lands first leaves the tx count
               // negative but cannot complete the phase without the leader's arrive).
               if (rank == 0) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * Cfg::STAGE);
               const uint32_t lf = leader_full0 + 8 * stage;
-              tma_load_2d_pair(sA + stage * Cfg::A_STAGE, &tmA, kx, a_row, lf, hint);
-              tma_load_2d_pair(sB + stage * Cfg::B_STAGE, &tmB, kx, b_row, lf, hint);
+#pragma unroll
+              for (int at = 0; at < Cfg::ATOMS; ++at) {
+                const int32_t x = kx + at * Cfg::ATOM_K;
+                tma_load_2d_pair(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM, &tmA, x, a_row, lf, hint);
+#pragma unroll
+                for (int h = 0; h < NH; ++h)
+                  tma_load_2d_pair(sB + stage * Cfg::B_STAGE + at * Cfg::B_ATOM + h * Cfg::B_HALF, &tmB, x,
+                                   b_row + h * Cfg::MMA_N, lf, hint);
+              }
             }
             ++issued;
             if (++stage == S) { stage = 0; phase ^= 1u; }
@@ -278,17 +313,11 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp == 1) {
     // ============================ MMA issuer (leader) ============================
     if (lane == 0 && rank == 0) {
-      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      uint32_t stage = 0, phase = 0, tile_iter = 0;
       bool ok = true;
       uint32_t tile = first_tile;
       bool more = tile < p.num_tiles;
       while (more && ok) {
-        if (!mbar_wait(bar_tempty + 8 * acc, acc_phase ^ 1u, p.wait_ns, abort_flag)) {
-          fail(ST_MMA_TMEM_EMPTY);
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * Cfg::BN;
         for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
           // TMA completion on the mbarrier makes the stage visible to the MMA; no
           // tcgen05 fence is needed between this wait and the MMAs.
@@ -300,19 +329,41 @@ __global__ void __launch_bounds__(256, 1)
           const uint32_t a0 = sA + stage * Cfg::A_STAGE;
           const uint32_t b0 = sB + stage * Cfg::B_STAGE;
 #pragma unroll
-          for (uint32_t k = 0; k < Cfg::KSTEPS; ++k) {
-            umma<CG, Cfg::KIND>(d_tmem, sdesc_k_sw128(a0 + 32u * k), sdesc_k_sw128(b0 + 32u * k),
-                                Cfg::IDESC, (kb | k) != 0u ? 1u : 0u);
+          for (int h = 0; h < NH; ++h) {
+            const uint32_t slot = acc_slot(tile_iter, h);
+            if (kb == 0) {
+              // the slot's previous contents must have been drained by the epilogue
+              if (!mbar_wait(bar_tempty + 8 * slot, (acc_use(tile_iter) & 1u) ^ 1u, p.wait_ns,
+                             abort_flag)) {
+                fail(ST_MMA_TMEM_EMPTY);
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint32_t d_tmem = tmem_base + slot * Cfg::MMA_N;
+#pragma unroll
+            for (uint32_t k = 0; k < Cfg::KSTEPS; ++k) {
+              const uint32_t a_k = a0 + (k / 4) * Cfg::A_ATOM + 32u * (k % 4);
+              const uint32_t b_k = b0 + (k / 4) * Cfg::B_ATOM + h * Cfg::B_HALF + 32u * (k % 4);
+              umma<CG, Cfg::KIND>(d_tmem, sdesc_k_sw128(a_k), sdesc_k_sw128(b_k), Cfg::IDESC,
+                                  (kb | k) != 0u ? 1u : 0u);
+            }
           }
+          if (!ok) break;
           // frees this stage in both CTAs once the MMAs above have read it
           if constexpr (CG == 1) umma_commit<1>(bar_empty + 8 * stage);
           else umma_commit_pair(bar_empty + 8 * stage, 0x3);
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        if constexpr (CG == 1) umma_commit<1>(bar_tfull + 8 * acc);
-        else umma_commit_pair(bar_tfull + 8 * acc, 0x3);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          const uint32_t slot = acc_slot(tile_iter, h);
+          if constexpr (CG == 1) umma_commit<1>(bar_tfull + 8 * slot);
+          else umma_commit_pair(bar_tfull + 8 * slot, 0x3);
+        }
+        ++tile_iter;
         if constexpr (SCHED == SCHED_CLC) {
           more = clc_next(tile);
         } else {
@@ -371,92 +422,100 @@ __global__ void __launch_bounds__(256, 1)
     if (p.scale_b) scale *= __ldg(p.scale_b);
     const uint32_t my_buf0 = sEpi + q * 2 * Cfg::EPI_BUF;
     const uint32_t leader_tempty0 = (CG == 2) ? mapa_shared(bar_tempty, 0) : bar_tempty;
-    uint32_t acc = 0, acc_phase = 0, buf = 0;
+    uint32_t tile_iter = 0, buf = 0;
     uint32_t tile = first_tile;
     bool more = tile < p.num_tiles;
-    while (more) {
+    bool ok = true;
+    while (more && ok) {
       uint32_t bm, bn;
       tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
-      uint32_t okw = 0;
-      if (lane == 0) {
-        // The accumulator takes a whole main loop to fill: sleep between polls
-        // (bounded by the same deadline and abort flag as every other wait).
-        const uint64_t t0 = globaltimer_ns();
-        bool done;
-        while (!(done = mbar_try_wait(bar_tfull + 8 * acc, acc_phase))) {
-          if (*abort_flag || globaltimer_ns() - t0 > p.wait_ns) break;
-          __nanosleep(1000);
-        }
-        okw = done ? 1u : 0u;
-      }
-      okw = __shfl_sync(0xffffffffu, okw, 0);
-      if (!okw) {
-        if (lane == 0) fail(ST_EPI_TMEM_FULL);
-        break;
-      }
-      tc_fence_after();
       const int32_t row0 = int32_t((bm * CG + rank) * Cfg::BM + 32 * q);
-      const uint32_t t_row = tmem_base + ((32u * q) << 16) + acc * Cfg::BN;
 #pragma unroll 1
-      for (uint32_t c = 0; c < Cfg::EPI_CHUNKS; ++c) {
-        uint32_t w[32];
-        if constexpr (Cfg::CD_BYTES == 4) {
-          uint32_t r[32];
-          tmem_ld_x32(t_row + c * Cfg::EPI_COLS, r);
-          tmem_wait_ld();
+      for (int h = 0; h < NH; ++h) {
+        const uint32_t slot = acc_slot(tile_iter, h);
+        const uint32_t par = acc_use(tile_iter) & 1u;
+        uint32_t okw = 0;
+        if (lane == 0) {
+          // The accumulator takes a whole main loop to fill: sleep between polls
+          // (bounded by the same deadline and abort flag as every other wait).
+          const uint64_t t0 = globaltimer_ns();
+          bool done;
+          while (!(done = mbar_try_wait(bar_tfull + 8 * slot, par))) {
+            if (*abort_flag || globaltimer_ns() - t0 > p.wait_ns) break;
+            __nanosleep(1000);
+          }
+          okw = done ? 1u : 0u;
+        }
+        okw = __shfl_sync(0xffffffffu, okw, 0);
+        if (!okw) {
+          if (lane == 0) fail(ST_EPI_TMEM_FULL);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + ((32u * q) << 16) + slot * Cfg::MMA_N;
+#pragma unroll 1
+        for (uint32_t c = 0; c < Cfg::EPI_CHUNKS; ++c) {
+          uint32_t w[32];
+          if constexpr (Cfg::CD_BYTES == 4) {
+            uint32_t r[32];
+            tmem_ld_x32(t_row + c * Cfg::EPI_COLS, r);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(r[i]) * scale);
-        } else {
-          uint32_t r0[32], r1[32];
-          tmem_ld_x32(t_row + c * Cfg::EPI_COLS, r0);
-          tmem_ld_x32(t_row + c * Cfg::EPI_COLS + 32, r1);
-          tmem_wait_ld();
+            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(r[i]) * scale);
+          } else {
+            uint32_t r0[32], r1[32];
+            tmem_ld_x32(t_row + c * Cfg::EPI_COLS, r0);
+            tmem_ld_x32(t_row + c * Cfg::EPI_COLS + 32, r1);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float x0 = __uint_as_float(r0[2 * i]) * scale;
-            const float x1 = __uint_as_float(r0[2 * i + 1]) * scale;
-            const float y0 = __uint_as_float(r1[2 * i]) * scale;
-            const float y1 = __uint_as_float(r1[2 * i + 1]) * scale;
-            if constexpr (CD == DT_BF16) {
-              w[i] = pack_bf16x2(x0, x1);
-              w[16 + i] = pack_bf16x2(y0, y1);
-            } else {
-              w[i] = pack_f16x2(x0, x1);
-              w[16 + i] = pack_f16x2(y0, y1);
+            for (int i = 0; i < 16; ++i) {
+              const float x0 = __uint_as_float(r0[2 * i]) * scale;
+              const float x1 = __uint_as_float(r0[2 * i + 1]) * scale;
+              const float y0 = __uint_as_float(r1[2 * i]) * scale;
+              const float y1 = __uint_as_float(r1[2 * i + 1]) * scale;
+              if constexpr (CD == DT_BF16) {
+                w[i] = pack_bf16x2(x0, x1);
+                w[16 + i] = pack_bf16x2(y0, y1);
+              } else {
+                w[i] = pack_f16x2(x0, x1);
+                w[16 + i] = pack_f16x2(y0, y1);
+              }
             }
           }
-        }
-        if (c == Cfg::EPI_CHUNKS - 1) {
-          // All TMEM reads of this accumulator are done: hand it back to the MMA warp.
-          tc_fence_before();
+          if (c == Cfg::EPI_CHUNKS - 1) {
+            // All TMEM reads of this slot are done: hand it back to the MMA warp.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (CG == 1) mbar_arrive(bar_tempty + 8 * slot);
+              else mbar_arrive_cluster(leader_tempty0 + 8 * slot);
+            }
+          }
+          // Staging buffer `buf` was last read by the TMA store committed two chunks ago.
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          const uint32_t sb = my_buf0 + buf * Cfg::EPI_BUF;
+          const uint32_t row_addr = sb + lane * 128u;
+#pragma unroll
+          for (uint32_t j = 0; j < 8; ++j) {
+            st_shared_v4(row_addr + ((j ^ (lane & 7u)) << 4), w[4 * j], w[4 * j + 1], w[4 * j + 2],
+                         w[4 * j + 3]);
+          }
+          fence_proxy_async_shared();
           __syncwarp();
           if (lane == 0) {
-            if constexpr (CG == 1) mbar_arrive(bar_tempty + 8 * acc);
-            else mbar_arrive_cluster(leader_tempty0 + 8 * acc);
+            // Boxes that start past the end of C (ragged M/N) are skipped; a box that
+            // straddles the edge is clipped by the TMA unit.
+            const uint32_t col0 = bn * Cfg::BN + h * Cfg::MMA_N + c * Cfg::EPI_COLS;
+            if (uint32_t(row0) < p.M && col0 < p.N) tma_store_2d(&tmC, sb, int32_t(col0), row0);
+            bulk_commit();
           }
+          buf ^= 1u;
         }
-        // Staging buffer `buf` was last read by the TMA store committed two chunks ago.
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
-        const uint32_t sb = my_buf0 + buf * Cfg::EPI_BUF;
-        const uint32_t row_addr = sb + lane * 128u;
-#pragma unroll
-        for (uint32_t j = 0; j < 8; ++j) {
-          st_shared_v4(row_addr + ((j ^ (lane & 7u)) << 4), w[4 * j], w[4 * j + 1], w[4 * j + 2],
-                       w[4 * j + 3]);
-        }
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          // Boxes that start past the end of C (ragged M/N) are skipped; a box that
-          // straddles the edge is clipped by the TMA unit.
-          const uint32_t col0 = bn * Cfg::BN + c * Cfg::EPI_COLS;
-          if (uint32_t(row0) < p.M && col0 < p.N) tma_store_2d(&tmC, sb, int32_t(col0), row0);
-          bulk_commit();
-        }
-        buf ^= 1u;
       }
-      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      if (!ok) break;
+      ++tile_iter;
       if constexpr (SCHED == SCHED_CLC) {
         uint32_t nt = tile;
         bool got = false;

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define B200GEMM_ABI_VERSION 1
+#define B200GEMM_ABI_VERSION 2
 
 /* element types */
 enum {
@@ -45,8 +45,8 @@ enum {
 enum {
   B200_VARIANT_AUTO = 0,       /* library picks                                        */
   B200_VARIANT_1CTA = 1,       /* one 128x256 tile per CTA    (05_gemm gemm_ws)        */
-  B200_VARIANT_2CTA = 2,       /* cta_group::2 pair, 256x256 tile, persistent
-                                  static schedule            (06_cluster gemm_ws_cluster)*/
+  B200_VARIANT_2CTA = 2,       /* cta_group::2 pair, 256x256 or 256x512 tile,
+                                  persistent static schedule (06_cluster gemm_ws_cluster)*/
   B200_VARIANT_PERSISTENT = 3, /* 1-CTA, grid = SM count, static group-M schedule
                                                               (08_persistent persist)  */
   B200_VARIANT_CLC = 4,        /* 1-CTA, cluster-launch-control work stealing
@@ -84,6 +84,9 @@ typedef struct B200GemmArgs {
   int32_t fault_inject;    /* 0 in production; 1 = test hook: producer issues no loads,
                               so the bounded waits must report a device timeout          */
   uint64_t wait_limit_ns;  /* bound of each device wait, 0 = library default (1 s)       */
+  int32_t tile_n;          /* C columns per tile: 0 = library default, 256, or 512 (the
+                              512-wide tile exists for the pair variants only)          */
+  int32_t reserved;        /* must be 0                                                  */
 } B200GemmArgs;
 
 /* Launch C = scale_a*scale_b*A.B^T on `stream` (a cudaStream_t, NULL = legacy default). */
@@ -97,8 +100,9 @@ const char* b200_gemm_strerror(int code);
  * the raw bits in *bits when bits != NULL) or B200_ERR_CUDA. */
 int b200_gemm_status(void* stream, int clear, uint32_t* bits);
 
-/* Library facts: variant tile shape and stage limits, for hosts and tests.
- * Returns B200_OK or B200_ERR_INVALID_ARG. */
+/* Library facts: tile shape and stage limits of a variant at a tile width
+ * (`tile_n` in: 0 = the variant's default width; out: the width used), for hosts
+ * and tests. Returns B200_OK or B200_ERR_INVALID_ARG. */
 int b200_gemm_variant_info(int32_t variant, int32_t ab_dtype, int32_t* tile_m, int32_t* tile_n,
                            int32_t* max_stages, int32_t* default_stages);
 

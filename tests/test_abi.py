@@ -68,7 +68,7 @@ int main(void) {{
 
 def test_abi_version_and_strerror(b200):
     L = b200.lib()
-    assert L.b200_gemm_abi_version() == 1
+    assert L.b200_gemm_abi_version() == 2
     for code in (0, -1, -2, -3, -4, -5, -6, -7, -8):
         assert b200.strerror(code)
     assert "unknown" in b200.strerror(-99)
@@ -81,7 +81,14 @@ def test_variant_info(b200):
         assert info["max_stages"] == 4
     for v in ("2cta", "2cta_clc"):
         info = b200.variant_info(v, b200.DT_E4M3)
-        assert info["tile_m"] == 256 and info["tile_n"] == 256 and info["max_stages"] == 6
+        assert info["tile_m"] == 256 and info["tile_n"] == 256 and info["max_stages"] == 3
+    for v in ("2cta", "2cta_clc"):
+        info = b200.variant_info(v, b200.DT_BF16, tile_n=512)
+        assert info["tile_m"] == 256 and info["tile_n"] == 512 and info["max_stages"] == 4
+    with pytest.raises(b200.B200Error):
+        b200.variant_info("persistent", tile_n=512)  # 512-wide tiles are pair-only
+    with pytest.raises(b200.B200Error):
+        b200.variant_info("2cta", tile_n=384)
     with pytest.raises(b200.B200Error):
         b200.variant_info(0)  # AUTO has no fixed shape
     with pytest.raises(b200.B200Error):
@@ -118,6 +125,8 @@ def _args(b200, **kw):
     ({"group_m": -1}, -1),
     ({"stages": -2}, -1),
     ({"scale_a": 0x40002}, -3),
+    ({"tile_n": 384}, -1),
+    ({"reserved": 1}, -1),
 ])
 def test_validation_codes(b200, kw, code):
     assert b200.gemm_raw(_args(b200, **kw), 0) == code

@@ -23,7 +23,12 @@ from gemm_check import (TOL_16, TOL_E4M3, compare, make_inputs, out_to_f32, refe
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-ALL_VARIANTS = ["1cta", "persistent", "clc", "2cta", "2cta_clc"]
+# "<variant>_w": the same variant with 256x512 pair tiles (tile_n = 512)
+ALL_VARIANTS = ["1cta", "persistent", "clc", "2cta", "2cta_clc", "2cta_w", "2cta_clc_w"]
+
+
+def _variant(v):
+    return (v[:-2], 512) if v.endswith("_w") else (v, 0)
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -35,6 +40,8 @@ def _cuda():
 
 
 def _run(b200, inp, variant, out_dtype, reps=1, **kw):
+    variant, tile_n = _variant(variant)
+    kw.setdefault("tile_n", tile_n)
     a, b, sa, sb = to_device(inp, torch)
     outs = []
     for _ in range(reps):
@@ -54,6 +61,9 @@ def _run(b200, inp, variant, out_dtype, reps=1, **kw):
 @pytest.mark.parametrize("stages", [2, 3, 4])
 def test_ref_check_fp16_512(b200, oracle, variant, stages):
     """gemm_ws CHECK: 512x512x256 fp16, seeds 601/602, fp32 C, 1e-3/1e-3, x3."""
+    v, tn = _variant(variant)
+    if stages > b200.variant_info(v, tile_n=tn)["max_stages"]:
+        pytest.skip("deeper than this variant's shared-memory ring")
     inp = make_inputs(oracle, 512, 512, 256, "f16", 601, 602)
     ref = reference(oracle, inp)
     for got in _run(b200, inp, variant, "f32", reps=3, stages=stages):
@@ -74,7 +84,8 @@ def test_ref_check_fp8_512(b200, oracle, variant):
 @pytest.mark.parametrize("shape", [(512, 512, 256), (2048, 2048, 256)])
 @pytest.mark.parametrize("group_m", [1, 8])
 @pytest.mark.parametrize("variant,stages", [("persistent", 2), ("persistent", 4), ("clc", 4),
-                                            ("2cta", 6), ("2cta_clc", 3)])
+                                            ("2cta", 2), ("2cta", 3), ("2cta_clc", 3),
+                                            ("2cta_w", 2), ("2cta_w", 4), ("2cta_clc_w", 4)])
 def test_ref_check_fp8_persistent(b200, oracle, shape, group_m, variant, stages):
     """gemm_fp8_persist CHECK: seeds 1001/1002, single- and multi-wave, G in {1,8}."""
     M, N, K = shape
@@ -85,7 +96,7 @@ def test_ref_check_fp8_persistent(b200, oracle, shape, group_m, variant, stages)
         assert r.mismatches == 0 and np.isfinite(got).all(), (r.max_abs_err, r.max_rel_err)
 
 
-@pytest.mark.parametrize("variant", ["clc", "2cta_clc"])
+@pytest.mark.parametrize("variant", ["clc", "2cta_clc", "2cta_clc_w"])
 def test_ref_check_fp8_dynamic_queue(b200, oracle, variant):
     """gemm_fp8_bn128 CHECK (dynamic tile queue -> CLC): seeds 2001/2002, 2048x2048x256."""
     inp = make_inputs(oracle, 2048, 2048, 256, "e4m3", 2001, 2002)
@@ -114,7 +125,7 @@ def test_config2_fp16_2048(b200, oracle, variant):
     assert ok, info
 
 
-@pytest.mark.parametrize("variant", ["2cta", "persistent"])
+@pytest.mark.parametrize("variant", ["2cta", "persistent", "2cta_w"])
 def test_config3_bf16_8192_sampled(b200, oracle, variant):
     """bf16 8192^3, normal(0,1)*0.1 seeds 605/606; seeded row bands vs the oracle."""
     inp = make_inputs(oracle, 8192, 8192, 8192, "bf16", 605, 606, dist="normal")
@@ -145,7 +156,7 @@ def test_config4_e4m3_8192_scaled_sampled(b200, oracle):
 
 
 @pytest.mark.parametrize("M,N,K", [(8192, 8192, 1024), (8192, 8192, 4096), (256, 16384, 8192)])
-@pytest.mark.parametrize("variant", ["clc", "persistent", "2cta", "2cta_clc"])
+@pytest.mark.parametrize("variant", ["clc", "persistent", "2cta", "2cta_clc", "2cta_w", "2cta_clc_w"])
 def test_config5_persistent_sweep(b200, oracle, M, N, K, variant):
     inp = make_inputs(oracle, M, N, K, "e4m3", 907, 908, scaled=True)
     (got,) = _run(b200, inp, variant, "bf16", group_m=8)
@@ -175,7 +186,7 @@ def test_ragged_shapes(b200, oracle, variant, dtype, out, M, N, K):
     assert ok, info
 
 
-@pytest.mark.parametrize("variant", ["persistent", "2cta"])
+@pytest.mark.parametrize("variant", ["persistent", "2cta", "2cta_w"])
 def test_padded_leading_dims(b200, oracle, variant):
     M, N, K = 384, 512, 320
     inp = make_inputs(oracle, M, N, K, "bf16", 21, 22)
@@ -186,7 +197,8 @@ def test_padded_leading_dims(b200, oracle, variant):
     bp.copy_(b)
     cbig = torch.full((M, N + 24), 7.0, dtype=torch.bfloat16, device="cuda")
     c = cbig[:, :N]
-    b200.gemm(ap, bp, c, variant=variant)
+    v, tn = _variant(variant)
+    b200.gemm(ap, bp, c, variant=v, tile_n=tn)
     torch.cuda.synchronize()
     ok, info = compare(out_to_f32(c, torch), reference(oracle, inp), TOL_16)
     assert ok, info
@@ -222,8 +234,9 @@ def test_bounded_wait_reports_timeout_and_context_survives(b200, oracle):
     a, b, _, _ = to_device(inp, torch)
     c = torch.zeros((256, 256), dtype=torch.float16, device="cuda")
     b200.status()  # clear
-    for variant in ("1cta", "2cta", "clc", "2cta_clc"):
-        b200.gemm(a, b, c, variant=variant, fault_inject=1, wait_limit_ns=10_000_000)
+    for variant in ("1cta", "2cta", "clc", "2cta_clc", "2cta_w"):
+        v, tn = _variant(variant)
+        b200.gemm(a, b, c, variant=v, tile_n=tn, fault_inject=1, wait_limit_ns=10_000_000)
         rc, bits = b200.status()
         assert rc == b200.ERR_DEVICE_TIMEOUT, (variant, rc, hex(bits))
         assert bits & 0x80000000
