@@ -34,6 +34,7 @@ ERR_LAUNCH = -5
 ERR_DEVICE_TIMEOUT = -6
 ERR_UNSUPPORTED = -7
 ERR_CUDA = -8
+ERR_SCRATCH_LIMIT = -9
 
 # Symbols declared in include/b200gemm.h (tests check the library exports them all).
 EXPORTS = [
@@ -44,6 +45,7 @@ EXPORTS = [
     "b200_gemm_pick_variant",
     "b200_quantize_e4m3",
     "b200_gemm_abi_version",
+    "b200_gemm_noalloc",
 ]
 
 

@@ -38,8 +38,8 @@ NVFLAGS = ARCH + [
     f"-I{CSRC}",
 ]
 
-LIB_SOURCES = ["b200gemm.cu", "inst_f16.cu", "inst_bf16.cu", "inst_e4m3.cu", "quant.cu"]
-HEADERS = ["sm100_ptx.cuh", "gemm_sm100.cuh", "gemm_launch.cuh"]
+LIB_SOURCES = ["b200gemm.cu", "inst_f16.cu", "inst_bf16.cu", "inst_e4m3.cu", "quant.cu", "noalloc.cu"]
+HEADERS = ["sm100_ptx.cuh", "gemm_sm100.cuh", "gemm_launch.cuh", "gemm_internal.h"]
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:

@@ -15,6 +15,7 @@
 #include <mutex>
 
 #include "b200gemm.h"
+#include "gemm_internal.h"
 #include "gemm_launch.cuh"
 
 namespace {
@@ -180,6 +181,103 @@ int pick_variant(const B200GemmArgs* a, int sms) {
 
 }  // namespace
 
+namespace b200 {
+
+// Launch body shared by the C-ABI entry points: `a` is validated and non-empty,
+// `sms` / `cc_major` describe the current device, and `status` is the device word
+// the kernel's bounded waits report into.
+int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc_major,
+                     uint32_t* status) {
+  int rc = B200_OK;
+  if (cc_major != 10) return B200_ERR_UNSUPPORTED;
+  const int ec = elem_bytes(a.c_dtype);
+
+  if (a.K == 0) {  // empty reduction: C = 0
+    cudaError_t e = cudaMemset2DAsync(a.C, size_t(a.ldc) * ec, 0, size_t(a.N) * ec, size_t(a.M), stream);
+    return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  }
+
+  const int variant = (a.variant == B200_VARIANT_AUTO) ? pick_variant(&a, sms) : a.variant;
+  VariantShape vs;
+  rc = variant_shape(variant, a.tile_n, &vs);
+  if (rc != B200_OK) return rc;
+  const uint32_t stages = a.stages ? uint32_t(a.stages) : vs.default_stages;
+  if (stages < 2 || stages > vs.max_stages) return B200_ERR_INVALID_ARG;
+
+  // K per TMA box (one 128-byte atom) and per pipeline stage (atoms x box)
+  const uint32_t bk = (a.ab_dtype == B200_DT_E4M3) ? 128u : 64u;
+  const uint32_t stage_k = bk * vs.atoms;
+  const uint32_t cd_cols = 128u / uint32_t(ec);
+
+  alignas(64) CUtensorMap tA, tB, tC;
+  rc = encode_2d(&tA, a.A, a.ab_dtype, uint64_t(a.M), uint64_t(a.K), uint64_t(a.lda), 128u, bk);
+  if (rc != B200_OK) return rc;
+  rc = encode_2d(&tB, a.B, a.ab_dtype, uint64_t(a.N), uint64_t(a.K), uint64_t(a.ldb),
+                 256u / uint32_t(vs.cg), bk);
+  if (rc != B200_OK) return rc;
+  rc = encode_2d(&tC, a.C, a.c_dtype, uint64_t(a.M), uint64_t(a.N), uint64_t(a.ldc), 32u, cd_cols);
+  if (rc != B200_OK) return rc;
+
+  KParams kp;
+  std::memset(&kp, 0, sizeof(kp));
+  kp.M = uint32_t(a.M);
+  kp.N = uint32_t(a.N);
+  kp.K = uint32_t(a.K);
+  kp.m_tiles = uint32_t((a.M + vs.tile_m - 1) / vs.tile_m);
+  kp.n_tiles = uint32_t((a.N + vs.tile_n - 1) / vs.tile_n);
+  const uint64_t tiles = uint64_t(kp.m_tiles) * kp.n_tiles;
+  if (tiles > 0x7fffffffull / 2) return B200_ERR_SHAPE;
+  kp.num_tiles = uint32_t(tiles);
+  kp.k_blocks = uint32_t((a.K + stage_k - 1) / stage_k);
+  kp.stages = stages;
+  kp.group_m = a.group_m ? uint32_t(a.group_m) : uint32_t(kDefaultGroupM);
+  kp.fault_inject = a.fault_inject ? 1u : 0u;
+  kp.scale_a = a.scale_a;
+  kp.scale_b = a.scale_b;
+  kp.status = status;
+  kp.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kDefaultWaitNs;
+
+  const uint32_t n_sms = uint32_t(sms);
+  uint32_t grid = 0;
+  switch (variant) {
+    case B200_VARIANT_1CTA:
+    case B200_VARIANT_CLC: grid = kp.num_tiles; break;
+    case B200_VARIANT_PERSISTENT: grid = kp.num_tiles < n_sms ? kp.num_tiles : n_sms; break;
+    case B200_VARIANT_2CTA: {
+      const uint32_t pairs = n_sms / 2;
+      grid = 2u * (kp.num_tiles < pairs ? kp.num_tiles : pairs);
+      break;
+    }
+    case B200_VARIANT_2CTA_CLC: grid = 2u * kp.num_tiles; break;
+    default: return B200_ERR_INVALID_ARG;
+  }
+
+  LaunchPlan lp;
+  lp.a = &tA;
+  lp.b = &tB;
+  lp.c = &tC;
+  lp.kp = kp;
+  lp.grid = grid;
+  lp.stream = stream;
+  // smem_bytes() depends only on the stage size, identical for every dtype.
+  lp.smem = variant_smem(vs, stages);
+
+  cudaError_t e;
+  switch (a.ab_dtype) {
+    case B200_DT_F16: e = b200::launch_f16(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
+    case B200_DT_BF16: e = b200::launch_bf16(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
+    default: e = b200::launch_e4m3(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
+  }
+  if (e == cudaErrorNotSupported) return B200_ERR_UNSUPPORTED;
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return B200_ERR_LAUNCH;
+  }
+  return B200_OK;
+}
+
+}  // namespace b200
+
 extern "C" {
 
 int b200_gemm_abi_version(void) { return B200GEMM_ABI_VERSION; }
@@ -195,6 +293,8 @@ const char* b200_gemm_strerror(int code) {
     case B200_ERR_DEVICE_TIMEOUT: return "a bounded device wait timed out";
     case B200_ERR_UNSUPPORTED: return "unsupported dtype/variant or device (needs sm_100)";
     case B200_ERR_CUDA: return "CUDA runtime error";
+    case B200_ERR_SCRATCH_LIMIT:
+      return "request needs more scratch than the allocation-free entry point's static array holds";
     default: return "unknown error code";
   }
 }
@@ -266,91 +366,7 @@ int b200_gemm(const B200GemmArgs* args, void* stream_v) {
   int dev = 0;
   rc = device_setup(&dev);
   if (rc != B200_OK) return rc;
-  if (g_cc_major[dev] != 10) return B200_ERR_UNSUPPORTED;
-  const int ec = elem_bytes(a.c_dtype);
-
-  if (a.K == 0) {  // empty reduction: C = 0
-    cudaError_t e = cudaMemset2DAsync(a.C, size_t(a.ldc) * ec, 0, size_t(a.N) * ec, size_t(a.M), stream);
-    return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
-  }
-
-  const int variant = (a.variant == B200_VARIANT_AUTO) ? pick_variant(&a, g_sm_count[dev]) : a.variant;
-  VariantShape vs;
-  rc = variant_shape(variant, a.tile_n, &vs);
-  if (rc != B200_OK) return rc;
-  const uint32_t stages = a.stages ? uint32_t(a.stages) : vs.default_stages;
-  if (stages < 2 || stages > vs.max_stages) return B200_ERR_INVALID_ARG;
-
-  // K per TMA box (one 128-byte atom) and per pipeline stage (atoms x box)
-  const uint32_t bk = (a.ab_dtype == B200_DT_E4M3) ? 128u : 64u;
-  const uint32_t stage_k = bk * vs.atoms;
-  const uint32_t cd_cols = 128u / uint32_t(ec);
-
-  alignas(64) CUtensorMap tA, tB, tC;
-  rc = encode_2d(&tA, a.A, a.ab_dtype, uint64_t(a.M), uint64_t(a.K), uint64_t(a.lda), 128u, bk);
-  if (rc != B200_OK) return rc;
-  rc = encode_2d(&tB, a.B, a.ab_dtype, uint64_t(a.N), uint64_t(a.K), uint64_t(a.ldb),
-                 256u / uint32_t(vs.cg), bk);
-  if (rc != B200_OK) return rc;
-  rc = encode_2d(&tC, a.C, a.c_dtype, uint64_t(a.M), uint64_t(a.N), uint64_t(a.ldc), 32u, cd_cols);
-  if (rc != B200_OK) return rc;
-
-  KParams kp;
-  std::memset(&kp, 0, sizeof(kp));
-  kp.M = uint32_t(a.M);
-  kp.N = uint32_t(a.N);
-  kp.K = uint32_t(a.K);
-  kp.m_tiles = uint32_t((a.M + vs.tile_m - 1) / vs.tile_m);
-  kp.n_tiles = uint32_t((a.N + vs.tile_n - 1) / vs.tile_n);
-  const uint64_t tiles = uint64_t(kp.m_tiles) * kp.n_tiles;
-  if (tiles > 0x7fffffffull / 2) return B200_ERR_SHAPE;
-  kp.num_tiles = uint32_t(tiles);
-  kp.k_blocks = uint32_t((a.K + stage_k - 1) / stage_k);
-  kp.stages = stages;
-  kp.group_m = a.group_m ? uint32_t(a.group_m) : uint32_t(kDefaultGroupM);
-  kp.fault_inject = a.fault_inject ? 1u : 0u;
-  kp.scale_a = a.scale_a;
-  kp.scale_b = a.scale_b;
-  kp.status = g_status[dev];
-  kp.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kDefaultWaitNs;
-
-  const uint32_t sms = uint32_t(g_sm_count[dev]);
-  uint32_t grid = 0;
-  switch (variant) {
-    case B200_VARIANT_1CTA:
-    case B200_VARIANT_CLC: grid = kp.num_tiles; break;
-    case B200_VARIANT_PERSISTENT: grid = kp.num_tiles < sms ? kp.num_tiles : sms; break;
-    case B200_VARIANT_2CTA: {
-      const uint32_t pairs = sms / 2;
-      grid = 2u * (kp.num_tiles < pairs ? kp.num_tiles : pairs);
-      break;
-    }
-    case B200_VARIANT_2CTA_CLC: grid = 2u * kp.num_tiles; break;
-    default: return B200_ERR_INVALID_ARG;
-  }
-
-  LaunchPlan lp;
-  lp.a = &tA;
-  lp.b = &tB;
-  lp.c = &tC;
-  lp.kp = kp;
-  lp.grid = grid;
-  lp.stream = stream;
-  // smem_bytes() depends only on the stage size, identical for every dtype.
-  lp.smem = variant_smem(vs, stages);
-
-  cudaError_t e;
-  switch (a.ab_dtype) {
-    case B200_DT_F16: e = b200::launch_f16(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
-    case B200_DT_BF16: e = b200::launch_bf16(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
-    default: e = b200::launch_e4m3(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
-  }
-  if (e == cudaErrorNotSupported) return B200_ERR_UNSUPPORTED;
-  if (e != cudaSuccess) {
-    (void)cudaGetLastError();
-    return B200_ERR_LAUNCH;
-  }
-  return B200_OK;
+  return b200::gemm_launch_impl(a, stream, g_sm_count[dev], g_cc_major[dev], g_status[dev]);
 }
 
 int b200_gemm_status(void* stream_v, int clear, uint32_t* bits) {
@@ -370,3 +386,14 @@ int b200_gemm_status(void* stream_v, int clear, uint32_t* bits) {
 }
 
 }  // extern "C"
+
+namespace b200 {
+
+int gemm_validate(const B200GemmArgs* a) { return validate(a); }
+
+int gemm_resolve_driver() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return resolve_encode();
+}
+
+}  // namespace b200

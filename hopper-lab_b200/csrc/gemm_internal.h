@@ -1,0 +1,24 @@
+// gemm_internal.h — host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "b200gemm.h"
+
+namespace b200 {
+
+// Argument checks that need no GPU (same codes as b200_gemm).
+int gemm_validate(const B200GemmArgs* a);
+
+// Resolve the driver's tensor-map encoder once per process (allocates nothing).
+int gemm_resolve_driver();
+
+// Launch body shared by the entry points: `a` is validated with M, N > 0; `sms`
+// and `cc_major` describe the current device; `status` is the device word the
+// kernel's bounded waits report into.
+int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc_major,
+                     uint32_t* status);
+
+}  // namespace b200

@@ -65,7 +65,9 @@ enum {
   B200_ERR_LAUNCH = -5,        /* CUDA launch / attribute error                        */
   B200_ERR_DEVICE_TIMEOUT = -6,/* a bounded device wait gave up (see b200_gemm_status) */
   B200_ERR_UNSUPPORTED = -7,   /* dtype/variant combination not built, or not sm_100   */
-  B200_ERR_CUDA = -8           /* other CUDA runtime error                             */
+  B200_ERR_CUDA = -8,          /* other CUDA runtime error                             */
+  B200_ERR_SCRATCH_LIMIT = -9  /* b200_gemm_noalloc: request needs more scratch than its
+                                  static device array holds                             */
 };
 
 typedef struct B200GemmArgs {
@@ -108,6 +110,21 @@ int b200_gemm_variant_info(int32_t variant, int32_t ab_dtype, int32_t* tile_m, i
 
 /* The variant B200_VARIANT_AUTO resolves to for this problem on the current device. */
 int b200_gemm_pick_variant(const B200GemmArgs* args);
+
+/* Allocation-free form of b200_gemm, for callers that cannot have a library call
+ * cudaMalloc: code inside frameworks whose pool allocator must own every device
+ * allocation, processes whose device footprint is fixed after start-up, and paths
+ * that must not take the allocator's locks. Same arguments, kernels and results as
+ * b200_gemm. The kernel's scratch (its status word) lives in a 256-byte static
+ * device array that every GPU loading the library holds until exit; a request
+ * needing more scratch returns B200_ERR_SCRATCH_LIMIT (the GEMM needs 4 bytes for
+ * every shape). All calls share that array and each call clears its word first,
+ * so calls that overlap on the GPU race on the status. The first call on a device
+ * looks up the array's device address (do it before any stream capture). With
+ * check_status != 0 the call synchronises `stream` and returns
+ * B200_ERR_DEVICE_TIMEOUT if a bounded wait gave up. No counterpart in the
+ * reference. */
+int b200_gemm_noalloc(const B200GemmArgs* args, void* stream, int check_status);
 
 /* Per-tensor e4m3 quantiser on the device: *scale = amax(|x|)/448 (1 when all
  * x == 0) and q[i] = e4m3_rn_satfinite(x[i] / *scale). Device pointers: x (fp32,
