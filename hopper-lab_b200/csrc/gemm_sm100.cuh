@@ -20,14 +20,15 @@
 //                    -> SCHED_CLC: hardware cluster-launch-control work stealing
 //                    replaces the global atomic tile counter
 //
-// CTA = 256 threads, 8 warps:
+// CTA = 384 threads, 12 warps:
 //   warp 0      TMA producer (one lane): A/B k-blocks into an S-stage smem ring
 //               (one 128-byte K atom per stage for 1-CTA tiles, two for pairs)
 //   warp 1      TMEM owner + MMA issuer (one lane of the leader CTA)
 //   warp 2      CLC scheduler (one lane of the leader CTA; SCHED_CLC only)
 //   warp 3      idle
-//   warps 4-7   epilogue: TMEM -> registers -> (scale, narrow) -> swizzled smem ->
-//               TMA store; warp 4+q drains TMEM lanes 32q..32q+31
+//   warps 4-11  epilogue: TMEM -> registers -> (scale, narrow) -> swizzled smem ->
+//               TMA store; warp 4+4e+q drains TMEM lanes 32q..32q+31, columns of half
+//               e of each 256-column slot
 // TMEM holds two 256-column fp32 slots. A tile of NH = 1 half (BN = 256) uses one
 // slot, so the epilogue of tile t overlaps the main loop of tile t+1. A pair tile of
 // NH = 2 halves (256 x 512, two N=256 MMAs per K-step sharing the A tiles, 25% less
@@ -109,7 +110,11 @@ struct GemmCfg {
   static constexpr int EPI_COLS = 128 / CD_BYTES;      // C columns per 128-byte chunk
   static constexpr int EPI_CHUNKS = MMA_N / EPI_COLS; // per 256-column slot
   static constexpr uint32_t EPI_BUF = 32 * 128;        // 32 rows × 128 bytes
-  static constexpr uint32_t EPI_BYTES = 4 * 2 * EPI_BUF;
+  // Eight epilogue warps: warp 4 + 4e + q drains TMEM lane quarter q, column half e
+  // of each 256-column slot, staging through one 4 KB buffer of its own.
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int EPI_CHUNKS_PER_WARP = EPI_CHUNKS / 2;
+  static constexpr uint32_t EPI_BYTES = EPI_WARPS * EPI_BUF;
   static constexpr uint32_t TMEM_COLS = 512;           // two 256-column fp32 slots
   static constexpr uint32_t MMA_M = BM * CG;
   static constexpr uint32_t IDESC =
@@ -119,9 +124,9 @@ struct GemmCfg {
   static constexpr uint32_t ALIGN_SLACK = 1024;
   static constexpr uint32_t MAX_STAGES =
       (MAX_SMEM - EPI_BYTES - BAR_BYTES - ALIGN_SLACK) / STAGE;
-  static constexpr uint32_t NUM_THREADS = 256;
-  // CLC ring consumers per CTA: producer + MMA + 4 epilogue warps
-  static constexpr uint32_t SCHED_CONSUMERS = 6;
+  static constexpr uint32_t NUM_THREADS = 128 + 32 * EPI_WARPS;
+  // CLC ring consumers per CTA: producer + MMA + the epilogue warps
+  static constexpr uint32_t SCHED_CONSUMERS = 2 + EPI_WARPS;
 
   static uint32_t smem_bytes(uint32_t stages) {
     return stages * STAGE + EPI_BYTES + BAR_BYTES + ALIGN_SLACK;
@@ -131,7 +136,7 @@ struct GemmCfg {
 };
 
 template <int AB, int CD, int CG, int SCHED, int NH>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const KParams p) {
   using Cfg = GemmCfg<AB, CD, CG, SCHED, NH>;
@@ -172,7 +177,7 @@ __global__ void __launch_bounds__(256, 1)
     for (uint32_t a = 0; a < 2; ++a) {
       mbar_init(bar_tfull + 8 * a, 1);
       // every epilogue warp of the pair hands the accumulator back to the leader
-      mbar_init(bar_tempty + 8 * a, 4 * CG);
+      mbar_init(bar_tempty + 8 * a, Cfg::EPI_WARPS * CG);
       // leader: the try_cancel response (tx); peer: the leader's forwarding arrive
       mbar_init(bar_sfull + 8 * a, 1);
       // slot release: every consumer of the pair arrives on the leader's barrier
@@ -349,6 +354,12 @@ __global__ void __launch_bounds__(256, 1)
               umma<CG, Cfg::KIND>(d_tmem, sdesc_k_sw128(a_k), sdesc_k_sw128(b_k), Cfg::IDESC,
                                   (kb | k) != 0u ? 1u : 0u);
             }
+            if (kb + 1 == p.k_blocks) {
+              // Slot h is final once these MMAs complete: signal it now, so with two
+              // halves the epilogue drains slot 0 while the last half-1 MMAs run.
+              if constexpr (CG == 1) umma_commit<1>(bar_tfull + 8 * slot);
+              else umma_commit_pair(bar_tfull + 8 * slot, 0x3);
+            }
           }
           if (!ok) break;
           // frees this stage in both CTAs once the MMAs above have read it
@@ -357,12 +368,6 @@ __global__ void __launch_bounds__(256, 1)
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-#pragma unroll
-        for (int h = 0; h < NH; ++h) {
-          const uint32_t slot = acc_slot(tile_iter, h);
-          if constexpr (CG == 1) umma_commit<1>(bar_tfull + 8 * slot);
-          else umma_commit_pair(bar_tfull + 8 * slot, 0x3);
-        }
         ++tile_iter;
         if constexpr (SCHED == SCHED_CLC) {
           more = clc_next(tile);
@@ -416,13 +421,14 @@ __global__ void __launch_bounds__(256, 1)
     __syncwarp();
   } else if (warp >= 4) {
     // ================================ epilogue ================================
-    const uint32_t q = warp - 4;  // TMEM lane quarter == warp id % 4
+    const uint32_t q = (warp - 4) & 3u;  // TMEM lane quarter == warp id % 4
+    const uint32_t e = (warp - 4) >> 2;  // column half of each slot
     float scale = 1.0f;
     if (p.scale_a) scale *= __ldg(p.scale_a);
     if (p.scale_b) scale *= __ldg(p.scale_b);
-    const uint32_t my_buf0 = sEpi + q * 2 * Cfg::EPI_BUF;
+    const uint32_t my_buf = sEpi + (warp - 4) * Cfg::EPI_BUF;
     const uint32_t leader_tempty0 = (CG == 2) ? mapa_shared(bar_tempty, 0) : bar_tempty;
-    uint32_t tile_iter = 0, buf = 0;
+    uint32_t tile_iter = 0;
     uint32_t tile = first_tile;
     bool more = tile < p.num_tiles;
     bool ok = true;
@@ -436,15 +442,21 @@ __global__ void __launch_bounds__(256, 1)
         const uint32_t par = acc_use(tile_iter) & 1u;
         uint32_t okw = 0;
         if (lane == 0) {
-          // The accumulator takes a whole main loop to fill: sleep between polls
-          // (bounded by the same deadline and abort flag as every other wait).
-          const uint64_t t0 = globaltimer_ns();
-          bool done;
-          while (!(done = mbar_try_wait(bar_tfull + 8 * slot, par))) {
-            if (*abort_flag || globaltimer_ns() - t0 > p.wait_ns) break;
-            __nanosleep(1000);
+          if constexpr (NH == 1) {
+            // Double-buffered accumulator: the drain is off the MMA's critical path,
+            // so sleep between polls (bounded by the same deadline and abort flag).
+            const uint64_t t0 = globaltimer_ns();
+            bool done;
+            while (!(done = mbar_try_wait(bar_tfull + 8 * slot, par))) {
+              if (*abort_flag || globaltimer_ns() - t0 > p.wait_ns) break;
+              __nanosleep(1000);
+            }
+            okw = done ? 1u : 0u;
+          } else {
+            // Single-buffered accumulator: the next tile's MMAs wait for this drain,
+            // so wake on the barrier itself rather than on a sleep timer.
+            okw = mbar_wait(bar_tfull + 8 * slot, par, p.wait_ns, abort_flag) ? 1u : 0u;
           }
-          okw = done ? 1u : 0u;
         }
         okw = __shfl_sync(0xffffffffu, okw, 0);
         if (!okw) {
@@ -454,48 +466,43 @@ __global__ void __launch_bounds__(256, 1)
         }
         tc_fence_after();
         const uint32_t t_row = tmem_base + ((32u * q) << 16) + slot * Cfg::MMA_N;
-#pragma unroll 1
-        for (uint32_t c = 0; c < Cfg::EPI_CHUNKS; ++c) {
+        const uint32_t c0 = e * Cfg::EPI_CHUNKS_PER_WARP;
+        // Read every TMEM column this warp owns in the slot, then release the slot
+        // before converting: the next tile's MMAs into it can start meanwhile.
+        uint32_t r[Cfg::EPI_CHUNKS_PER_WARP][Cfg::EPI_COLS];
+#pragma unroll
+        for (int cc = 0; cc < Cfg::EPI_CHUNKS_PER_WARP; ++cc) {
+#pragma unroll
+          for (int x = 0; x < Cfg::EPI_COLS / 32; ++x) {
+            uint32_t (&rr)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[cc][32 * x]);
+            tmem_ld_x32(t_row + (c0 + cc) * Cfg::EPI_COLS + 32 * x, rr);
+          }
+        }
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 1) mbar_arrive(bar_tempty + 8 * slot);
+          else mbar_arrive_cluster(leader_tempty0 + 8 * slot);
+        }
+#pragma unroll
+        for (int cc = 0; cc < Cfg::EPI_CHUNKS_PER_WARP; ++cc) {
           uint32_t w[32];
           if constexpr (Cfg::CD_BYTES == 4) {
-            uint32_t r[32];
-            tmem_ld_x32(t_row + c * Cfg::EPI_COLS, r);
-            tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(r[i]) * scale);
+            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(__uint_as_float(r[cc][i]) * scale);
           } else {
-            uint32_t r0[32], r1[32];
-            tmem_ld_x32(t_row + c * Cfg::EPI_COLS, r0);
-            tmem_ld_x32(t_row + c * Cfg::EPI_COLS + 32, r1);
-            tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float x0 = __uint_as_float(r0[2 * i]) * scale;
-              const float x1 = __uint_as_float(r0[2 * i + 1]) * scale;
-              const float y0 = __uint_as_float(r1[2 * i]) * scale;
-              const float y1 = __uint_as_float(r1[2 * i + 1]) * scale;
-              if constexpr (CD == DT_BF16) {
-                w[i] = pack_bf16x2(x0, x1);
-                w[16 + i] = pack_bf16x2(y0, y1);
-              } else {
-                w[i] = pack_f16x2(x0, x1);
-                w[16 + i] = pack_f16x2(y0, y1);
-              }
+            for (int i = 0; i < 32; ++i) {
+              const float x0 = __uint_as_float(r[cc][2 * i]) * scale;
+              const float x1 = __uint_as_float(r[cc][2 * i + 1]) * scale;
+              if constexpr (CD == DT_BF16) w[i] = pack_bf16x2(x0, x1);
+              else w[i] = pack_f16x2(x0, x1);
             }
           }
-          if (c == Cfg::EPI_CHUNKS - 1) {
-            // All TMEM reads of this slot are done: hand it back to the MMA warp.
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-              if constexpr (CG == 1) mbar_arrive(bar_tempty + 8 * slot);
-              else mbar_arrive_cluster(leader_tempty0 + 8 * slot);
-            }
-          }
-          // Staging buffer `buf` was last read by the TMA store committed two chunks ago.
-          if (lane == 0) bulk_wait_read<1>();
+          if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
-          const uint32_t sb = my_buf0 + buf * Cfg::EPI_BUF;
+          const uint32_t sb = my_buf;
           const uint32_t row_addr = sb + lane * 128u;
 #pragma unroll
           for (uint32_t j = 0; j < 8; ++j) {
@@ -505,13 +512,10 @@ __global__ void __launch_bounds__(256, 1)
           fence_proxy_async_shared();
           __syncwarp();
           if (lane == 0) {
-            // Boxes that start past the end of C (ragged M/N) are skipped; a box that
-            // straddles the edge is clipped by the TMA unit.
-            const uint32_t col0 = bn * Cfg::BN + h * Cfg::MMA_N + c * Cfg::EPI_COLS;
+            const uint32_t col0 = bn * Cfg::BN + h * Cfg::MMA_N + (c0 + cc) * Cfg::EPI_COLS;
             if (uint32_t(row0) < p.M && col0 < p.N) tma_store_2d(&tmC, sb, int32_t(col0), row0);
             bulk_commit();
           }
-          buf ^= 1u;
         }
       }
       if (!ok) break;

@@ -2,6 +2,8 @@
 
   python hopper-lab_b200/profile_case.py <f16|e4m3> <ours|cublas> [variant] [size]
 
+size: S (M = N = K = S), MxK (N = M) or MxNxK.
+
 Three warm-up launches run first; ncu with --profile-from-start off then captures
 only the fourth. 'cublas' runs torch.matmul (fp16) or torch._scaled_mm (e4m3) on
 the same inputs as the reference column.
@@ -12,7 +14,12 @@ import __graft_entry__ as g
 b200 = g._load_pkg()
 dt, who = sys.argv[1], sys.argv[2]
 variant = sys.argv[3] if len(sys.argv) > 3 else 'auto'
-M = N = K = int(sys.argv[4]) if len(sys.argv) > 4 else 8192
+size = sys.argv[4] if len(sys.argv) > 4 else "8192"
+if "x" in size:  # MxK (N = M) or MxNxK
+    dims = [int(v) for v in size.split("x")]
+    M, N, K = (dims[0], dims[0], dims[1]) if len(dims) == 2 else dims
+else:
+    M = N = K = int(size)
 torch.cuda.set_device(0)
 g_ = torch.Generator(device='cuda'); g_.manual_seed(0)
 if dt == 'f16':
