@@ -6,6 +6,8 @@ reference's ``-gencode=arch=compute_90a,code=sm_90a`` (CMakeLists.txt:21).
 Objects go to ``hopper-lab_b200/_build/``; the shared library to
 ``hopper-lab_b200/lib/`` (in-tree, so it travels with the repository snapshot).
 
+Executables (one per reference experiment) go to ``hopper-lab_b200/bin/``.
+
 Usage: python hopper-lab_b200/build.py [--force] [-j N]
 """
 from __future__ import annotations
@@ -79,6 +81,39 @@ def build_library(force: bool = False, jobs: int = 8) -> Path:
     return so
 
 
+EXPERIMENTS = {
+    # executable: extra link libraries
+    "gemm_ws": [],
+    "gemm_cluster": [],
+    "gemm_fp8": [],
+    "gemm_persistent": [],
+    "peak_tcgen05": [],
+    "cublaslt_ref": ["-lcublasLt"],
+    "gemm_multi_gpu": ["-lnccl"],
+}
+
+
+def build_experiments(force: bool = False, jobs: int = 8) -> list[Path]:
+    """One executable per experiment (hopper-lab_b200/experiments/*.cu), linked
+    against lib/libb200gemm.so with an $ORIGIN-relative rpath."""
+    BIN.mkdir(exist_ok=True)
+    exp = PKG / "experiments"
+    so = LIB / "libb200gemm.so"
+    deps_common = [exp / "exp_common.h", so] + _headers() + sorted((ROOT / "include" / "common").glob("*.h"))
+    todo, outs = [], []
+    for name, libs in EXPERIMENTS.items():
+        src = exp / f"{name}.cu"
+        out = BIN / name
+        outs.append(out)
+        if force or _stale(out, [src] + deps_common):
+            todo.append([NVCC, *[f for f in NVFLAGS if f != "-std=c++17"], "-std=c++20", f"-I{exp}",
+                         str(src), "-o", str(out), f"-L{LIB}", "-lb200gemm", *libs,
+                         "-Xlinker", "-rpath", "-Xlinker", "$ORIGIN/../lib"])
+    with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
+        list(ex.map(_run, todo))
+    return outs
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -86,6 +121,8 @@ def main() -> None:
     a = ap.parse_args()
     so = build_library(force=a.force, jobs=a.j)
     print(so)
+    for b in build_experiments(force=a.force, jobs=a.j):
+        print(b)
 
 
 if __name__ == "__main__":
