@@ -235,6 +235,19 @@ __global__ void __launch_bounds__(384, 1)
     return got;
   };
 
+  // Next tile after `tile`, fetched by every role at the START of its current tile
+  // so that with CLC the ring slot is released a whole tile before the scheduler
+  // needs it again (at small K a tile is only a few pipeline stages long).
+  auto fetch_next = [&](uint32_t tile, uint32_t& next) -> bool {
+    if constexpr (SCHED == SCHED_CLC) {
+      next = tile;
+      return clc_next(next);
+    } else {
+      next = tile + tile_stride;
+      return next < p.num_tiles;
+    }
+  };
+
   if (warp == 0) {
     // =============================== TMA producer ===============================
     if (lane == 0) {
@@ -246,6 +259,8 @@ __global__ void __launch_bounds__(384, 1)
         uint32_t tile = first_tile;
         bool more = tile < p.num_tiles;
         while (more && ok) {
+          uint32_t next;
+          const bool next_more = fetch_next(tile, next);
           uint32_t bm, bn;
           tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
           const int32_t a_row = int32_t((bm * CG + rank) * Cfg::BM);
@@ -289,12 +304,8 @@ __global__ void __launch_bounds__(384, 1)
             if (++stage == S) { stage = 0; phase ^= 1u; }
           }
           if (!ok) break;
-          if constexpr (SCHED == SCHED_CLC) {
-            more = clc_next(tile);
-          } else {
-            tile += tile_stride;
-            more = tile < p.num_tiles;
-          }
+          tile = next;
+          more = next_more;
         }
       }
       if (!ok || *abort_flag) {
@@ -323,6 +334,8 @@ __global__ void __launch_bounds__(384, 1)
       uint32_t tile = first_tile;
       bool more = tile < p.num_tiles;
       while (more && ok) {
+        uint32_t next;
+        const bool next_more = fetch_next(tile, next);
         for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
           // TMA completion on the mbarrier makes the stage visible to the MMA; no
           // tcgen05 fence is needed between this wait and the MMAs.
@@ -369,12 +382,8 @@ __global__ void __launch_bounds__(384, 1)
         }
         if (!ok) break;
         ++tile_iter;
-        if constexpr (SCHED == SCHED_CLC) {
-          more = clc_next(tile);
-        } else {
-          tile += tile_stride;
-          more = tile < p.num_tiles;
-        }
+        tile = next;
+        more = next_more;
       }
       // Every MMA this thread issued must retire before TMEM is released.
       umma_commit<CG>(bar_done);
@@ -433,6 +442,16 @@ __global__ void __launch_bounds__(384, 1)
     bool more = tile < p.num_tiles;
     bool ok = true;
     while (more && ok) {
+      uint32_t next = tile;
+      bool next_more;
+      if constexpr (SCHED == SCHED_CLC) {
+        bool got = false;
+        if (lane == 0) got = clc_next(next);
+        next_more = __shfl_sync(0xffffffffu, got ? 1u : 0u, 0) != 0u;
+        next = __shfl_sync(0xffffffffu, next, 0);
+      } else {
+        next_more = fetch_next(tile, next);
+      }
       uint32_t bm, bn;
       tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
       const int32_t row0 = int32_t((bm * CG + rank) * Cfg::BM + 32 * q);
@@ -520,16 +539,8 @@ __global__ void __launch_bounds__(384, 1)
       }
       if (!ok) break;
       ++tile_iter;
-      if constexpr (SCHED == SCHED_CLC) {
-        uint32_t nt = tile;
-        bool got = false;
-        if (lane == 0) got = clc_next(nt);
-        more = __shfl_sync(0xffffffffu, got ? 1u : 0u, 0) != 0u;
-        tile = __shfl_sync(0xffffffffu, nt, 0);
-      } else {
-        tile += tile_stride;
-        more = tile < p.num_tiles;
-      }
+      tile = next;
+      more = next_more;
     }
     if (lane == 0) bulk_wait<0>();
     __syncwarp();
