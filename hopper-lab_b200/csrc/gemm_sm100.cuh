@@ -120,7 +120,11 @@ struct GemmCfg {
   static constexpr uint32_t IDESC =
       idesc_f32acc(AB == DT_BF16 ? 1u : 0u, AB == DT_BF16 ? 1u : 0u, MMA_M, MMA_N);
   static constexpr uint32_t MAX_SMEM = 232448;         // 227 KB opt-in per CTA
-  static constexpr uint32_t BAR_BYTES = 256;
+  static constexpr uint32_t BAR_BYTES = 512;
+  // CLC response ring depth: the scheduler may run this many tiles ahead of the
+  // slowest consumer (at small K a tile is only a few stages long, and a
+  // try_cancel round trip plus the pair forwarding must fit in the lead).
+  static constexpr uint32_t CLC_SLOTS = 4;
   static constexpr uint32_t ALIGN_SLACK = 1024;
   static constexpr uint32_t MAX_STAGES =
       (MAX_SMEM - EPI_BYTES - BAR_BYTES - ALIGN_SLACK) / STAGE;
@@ -154,17 +158,18 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t sEpi = base + S * Cfg::STAGE;
   const uint32_t sBar = sEpi + Cfg::EPI_BYTES;
   uint8_t* bar_ptr = base_ptr + (sBar - base);
-  // 8-byte barriers: full[8], empty[8], tfull[2], tempty[2], sfull[2], sempty[2], done
+  // 8-byte barriers: full[8], empty[8], tfull[2], tempty[2], sfull[4], sempty[4], done;
+  // then the CLC responses (4 × 16 B), the TMEM base address and the abort flag
   const uint32_t bar_full = sBar;
   const uint32_t bar_empty = sBar + 64;
   const uint32_t bar_tfull = sBar + 128;
   const uint32_t bar_tempty = sBar + 144;
   const uint32_t bar_sfull = sBar + 160;
-  const uint32_t bar_sempty = sBar + 176;
-  const uint32_t bar_done = sBar + 192;
-  const uint32_t clc_resp = sBar + 208;                 // 2 × 16 B
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 240);
-  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(bar_ptr + 244);
+  const uint32_t bar_sempty = sBar + 192;
+  const uint32_t bar_done = sBar + 224;
+  const uint32_t clc_resp = sBar + 240;                 // 4 × 16 B
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 304);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(bar_ptr + 308);
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
@@ -178,6 +183,8 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(bar_tfull + 8 * a, 1);
       // every epilogue warp of the pair hands the accumulator back to the leader
       mbar_init(bar_tempty + 8 * a, Cfg::EPI_WARPS * CG);
+    }
+    for (uint32_t a = 0; a < Cfg::CLC_SLOTS; ++a) {
       // leader: the try_cancel response (tx); peer: the leader's forwarding arrive
       mbar_init(bar_sfull + 8 * a, 1);
       // slot release: every consumer of the pair arrives on the leader's barrier
@@ -230,7 +237,7 @@ __global__ void __launch_bounds__(384, 1)
     const bool got = clc_decode(clc_resp + 16 * sched_slot, x);
     if constexpr (CG == 1) mbar_arrive(bar_sempty + 8 * sched_slot);
     else mbar_arrive_cluster(leader_sempty0 + 8 * sched_slot);
-    if (++sched_slot == 2) { sched_slot = 0; sched_phase ^= 1u; }
+    if (++sched_slot == Cfg::CLC_SLOTS) { sched_slot = 0; sched_phase ^= 1u; }
     if (got) tile = x / CG;
     return got;
   };
@@ -423,7 +430,7 @@ __global__ void __launch_bounds__(384, 1)
             mbar_arrive_cluster(peer_sfull0 + 8 * slot);
           }
           if (!got) break;  // grid exhausted: a failed request ends the schedule
-          if (++slot == 2) { slot = 0; ph ^= 1u; }
+          if (++slot == Cfg::CLC_SLOTS) { slot = 0; ph ^= 1u; }
         }
       }
     }
