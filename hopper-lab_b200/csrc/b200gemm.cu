@@ -12,6 +12,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "b200gemm.h"
@@ -30,6 +31,30 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 std::mutex g_mu;
+// stream-K partial-tile workspace: one 128 x 256 fp32 region and one ready flag per
+// CTA slot (256 slots cover any grid on a 148-SM part), allocated on first use
+constexpr int kSkSlots = 256;
+float* g_sk_work[64] = {nullptr};
+uint32_t* g_sk_flags[64] = {nullptr};
+std::atomic<uint32_t> g_sk_epoch[64];
+
+int streamk_workspace(int dev, float** work, uint32_t** flags) {
+  if (!g_sk_work[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_sk_work[dev]) {
+      float* w = nullptr;
+      uint32_t* f = nullptr;
+      if (cudaMalloc(&w, size_t(kSkSlots) * 128 * 256 * sizeof(float)) != cudaSuccess) return B200_ERR_CUDA;
+      if (cudaMalloc(&f, size_t(kSkSlots) * sizeof(uint32_t)) != cudaSuccess) return B200_ERR_CUDA;
+      if (cudaMemset(f, 0, size_t(kSkSlots) * sizeof(uint32_t)) != cudaSuccess) return B200_ERR_CUDA;
+      g_sk_flags[dev] = f;
+      g_sk_work[dev] = w;
+    }
+  }
+  *work = g_sk_work[dev];
+  *flags = g_sk_flags[dev];
+  return B200_OK;
+}
 EncodeTiledFn g_encode = nullptr;
 uint32_t* g_status[64] = {nullptr};
 int g_sm_count[64] = {0};
@@ -158,6 +183,10 @@ int variant_shape(int variant, int tile_n, VariantShape* vs) {
       if (wide) fill_shape<2, b200::SCHED_CLC, 2>(vs);
       else fill_shape<2, b200::SCHED_CLC, 1>(vs);
       break;
+    case B200_VARIANT_2CTA_STREAMK:
+      if (wide) return B200_ERR_INVALID_ARG;
+      fill_shape<2, b200::SCHED_STREAMK, 1>(vs);
+      break;
     default: return B200_ERR_INVALID_ARG;
   }
   return B200_OK;
@@ -182,14 +211,28 @@ int pick_tile_n(const B200GemmArgs* a, int variant, int sms) {
   return wide_tiles >= sms ? 512 : 256;
 }
 
-int pick_variant(const B200GemmArgs* a, int sms) {
+int pick_variant(const B200GemmArgs* a, int sms, bool allow_workspace) {
   const int64_t pair_tiles = ((a->M + 255) / 256) * ((a->N + 255) / 256);
-  // The pair variant halves each SM's B traffic; use it once there is at least
-  // half a wave of pair tiles. Small problems keep 1-CTA tiles for parallelism.
-  if (a->M >= 256 && pair_tiles * 2 >= sms) return B200_VARIANT_2CTA;
-  const int64_t tiles = ((a->M + 127) / 128) * ((a->N + 255) / 256);
-  if (tiles > sms) return B200_VARIANT_PERSISTENT;
-  return B200_VARIANT_1CTA;
+  const int64_t cta_tiles = ((a->M + 127) / 128) * ((a->N + 255) / 256);
+  const int64_t pairs = sms / 2;
+  // A pair computes the same 256 x 256 area per SM-pair-step as two 1-CTA tiles while
+  // reading each B row once per pair, so it wins whenever it needs no more waves than
+  // the 1-CTA tiling (it needs more only when M rounds up badly, e.g. M = 384).
+  const int64_t pair_waves = (pair_tiles + pairs - 1) / pairs;
+  const int64_t cta_waves = (cta_tiles + sms - 1) / sms;
+  if (a->M >= 256 && pair_waves <= cta_waves) {
+    // Stream-K only when the static pair schedule would leave three quarters of the
+    // pairs idle and K is long: each split tile costs a 128 KB fp32 partial written
+    // and read back through L2 per CTA, a few microseconds that only a long K loop
+    // repays (measured: 1024x1024x8192 f16 +23%, 1024x1024x16384 f16 +71% and e4m3
+    // +15%; 1024x1024x8192 e4m3, 2048^3 and 256x16384x8192 slower than static).
+    if (allow_workspace && pair_tiles * 4 <= pairs) {
+      const int64_t stage_k = (a->ab_dtype == B200_DT_E4M3) ? 256 : 128;
+      if ((a->K + stage_k - 1) / stage_k >= 48) return B200_VARIANT_2CTA_STREAMK;
+    }
+    return B200_VARIANT_2CTA;
+  }
+  return cta_tiles > sms ? B200_VARIANT_PERSISTENT : B200_VARIANT_1CTA;
 }
 
 }  // namespace
@@ -200,7 +243,7 @@ namespace b200 {
 // `sms` / `cc_major` describe the current device, and `status` is the device word
 // the kernel's bounded waits report into.
 int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc_major,
-                     uint32_t* status) {
+                     uint32_t* status, bool allow_workspace) {
   int rc = B200_OK;
   if (cc_major != 10) return B200_ERR_UNSUPPORTED;
   const int ec = elem_bytes(a.c_dtype);
@@ -210,7 +253,8 @@ int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc
     return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
   }
 
-  const int variant = (a.variant == B200_VARIANT_AUTO) ? pick_variant(&a, sms) : a.variant;
+  const int variant = (a.variant == B200_VARIANT_AUTO) ? pick_variant(&a, sms, allow_workspace) : a.variant;
+  if (variant == B200_VARIANT_2CTA_STREAMK && !allow_workspace) return B200_ERR_SCRATCH_LIMIT;
   VariantShape vs;
   const int tile_n = a.tile_n ? a.tile_n : pick_tile_n(&a, variant, sms);
   rc = variant_shape(variant, tile_n, &vs);
@@ -263,6 +307,22 @@ int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc
       break;
     }
     case B200_VARIANT_2CTA_CLC: grid = 2u * kp.num_tiles; break;
+    case B200_VARIANT_2CTA_STREAMK: {
+      // every pair must be resident at once (a split tile's last owner waits for
+      // the partial sums of the earlier owners), so at most one pair per SM pair
+      const uint64_t iters = uint64_t(kp.num_tiles) * kp.k_blocks;
+      const uint32_t pairs = n_sms / 2;
+      const uint32_t workers = uint32_t(iters < pairs ? iters : pairs);
+      grid = 2u * workers;
+      int dev = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B200_ERR_CUDA;
+      rc = streamk_workspace(dev, &kp.sk_work, &kp.sk_flags);
+      if (rc != B200_OK) return rc;
+      uint32_t ep = g_sk_epoch[dev].fetch_add(1) + 1;
+      if (ep == 0) ep = g_sk_epoch[dev].fetch_add(1) + 1;  // 0 is the flags' initial value
+      kp.sk_epoch = ep;
+      break;
+    }
     default: return B200_ERR_INVALID_ARG;
   }
 
@@ -334,7 +394,7 @@ static int validate(const B200GemmArgs* a) {
     return B200_ERR_INVALID_ARG;
   if (a->c_dtype != B200_DT_F16 && a->c_dtype != B200_DT_BF16 && a->c_dtype != B200_DT_F32)
     return B200_ERR_INVALID_ARG;
-  if (a->variant < B200_VARIANT_AUTO || a->variant > B200_VARIANT_2CTA_CLC) return B200_ERR_INVALID_ARG;
+  if (a->variant < B200_VARIANT_AUTO || a->variant > B200_VARIANT_2CTA_STREAMK) return B200_ERR_INVALID_ARG;
   if (a->M < 0 || a->N < 0 || a->K < 0) return B200_ERR_SHAPE;
   // TMA coordinates are int32 and the tile counters are uint32.
   const int64_t lim = (int64_t(1) << 31) - 1;
@@ -368,7 +428,7 @@ int b200_gemm_pick_variant(const B200GemmArgs* args) {
   int dev = 0;
   rc = device_setup(&dev);
   if (rc != B200_OK) return rc;
-  return pick_variant(args, g_sm_count[dev]);
+  return pick_variant(args, g_sm_count[dev], true);
 }
 
 int b200_gemm(const B200GemmArgs* args, void* stream_v) {

@@ -18,7 +18,10 @@ int gemm_resolve_driver();
 // Launch body shared by the entry points: `a` is validated with M, N > 0; `sms`
 // and `cc_major` describe the current device; `status` is the device word the
 // kernel's bounded waits report into.
+// `allow_workspace` = false keeps the launch away from every schedule that needs
+// library-owned device memory (stream-K): AUTO never picks it, an explicit request
+// returns B200_ERR_SCRATCH_LIMIT.
 int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc_major,
-                     uint32_t* status);
+                     uint32_t* status, bool allow_workspace = true);
 
 }  // namespace b200

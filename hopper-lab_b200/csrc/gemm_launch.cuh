@@ -47,6 +47,19 @@ cudaError_t launch_gemm(const LaunchPlan& lp) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
+  if (SCHED == SCHED_STREAMK) {
+    // A split tile's last owner waits for the earlier owners' partial sums, so the
+    // whole grid must be resident at once: clamp it to the clusters that fit.
+    static int max_clusters[64] = {0};
+    if (!max_clusters[dev]) {
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return e;
+      if (n < 1) return cudaErrorInvalidConfiguration;
+      max_clusters[dev] = n;
+    }
+    if (cfg.gridDim.x > uint32_t(max_clusters[dev]) * CG) cfg.gridDim.x = uint32_t(max_clusters[dev]) * CG;
+  }
   return cudaLaunchKernelEx(&cfg, kern, *lp.a, *lp.b, *lp.c, lp.kp);
 }
 
@@ -71,6 +84,7 @@ cudaError_t launch_e4m3(int cd, int cg, int sched, int nh, const LaunchPlan& lp)
     } else if (cg == 2 && nh == 1) {                                                     \
       if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 1);               \
       if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 1);                     \
+      if (sched == SCHED_STREAMK) B200_DISPATCH_CD(AB, 2, SCHED_STREAMK, 1);             \
     } else if (cg == 2 && nh == 2) {                                                     \
       if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 2);               \
       if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 2);                     \

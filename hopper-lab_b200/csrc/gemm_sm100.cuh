@@ -41,7 +41,7 @@
 namespace b200 {
 
 enum : int { DT_F16 = 0, DT_BF16 = 1, DT_E4M3 = 2, DT_F32 = 3 };
-enum : int { SCHED_STATIC = 0, SCHED_CLC = 1 };
+enum : int { SCHED_STATIC = 0, SCHED_CLC = 1, SCHED_STREAMK = 2 };
 
 // Bits OR-ed into the device status word when a bounded wait gives up.
 enum : uint32_t {
@@ -51,6 +51,7 @@ enum : uint32_t {
   ST_EPI_TMEM_FULL = 1u << 3,
   ST_SCHED = 1u << 4,
   ST_DRAIN = 1u << 5,
+  ST_STREAMK = 1u << 6,
   ST_ABORTED = 1u << 31,
 };
 
@@ -67,6 +68,22 @@ struct KParams {
   const float* scale_b;
   uint32_t* status;       // device status word, may be null
   uint64_t wait_ns;       // bound of every mbarrier wait
+  // SCHED_STREAMK only: fp32 partial-tile workspace (one 128 x 256 region per CTA
+  // slot), per-slot ready flags, and this launch's epoch (the value a ready flag
+  // holds; flags never need resetting between launches)
+  float* sk_work;
+  uint32_t* sk_flags;
+  uint32_t sk_epoch;
+};
+
+// A unit of work of one CTA (pair): k-blocks [kb0, kb1) of a tile.
+//   FULL    the whole K range: store C
+//   PARTIAL the range ends inside the tile: write fp32 partial sums, raise the flag
+//   LAST    the range ends the tile but starts inside it: add the partials of the
+//           workers that own the earlier part of the tile, then store C
+enum : uint32_t { ITEM_FULL = 0, ITEM_PARTIAL = 1, ITEM_LAST = 2 };
+struct WorkItem {
+  uint32_t tile, kb0, kb1, kind, idx;
 };
 
 // Linear tile id -> (block-row, block-col) in group-M order. Same mapping as the
@@ -136,6 +153,9 @@ struct GemmCfg {
     return stages * STAGE + EPI_BYTES + BAR_BYTES + ALIGN_SLACK;
   }
   static_assert(NH == 1 || (NH == 2 && CG == 2), "512-wide tiles are built for CTA pairs");
+  static_assert(SCHED != SCHED_STREAMK || NH == 1, "stream-K uses 256-wide tiles");
+  // stream-K partial of one CTA: 128 rows x 256 fp32 columns
+  static constexpr uint32_t SK_FLOATS = BM * MMA_N;
   static_assert(MAX_STAGES <= 8, "the barrier block holds 8 ring stages");
 };
 
@@ -170,6 +190,7 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t clc_resp = sBar + 240;                 // 4 × 16 B
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 304);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(bar_ptr + 308);
+  const uint32_t bar_skdone = sBar + 320;               // stream-K: partial written
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
@@ -191,6 +212,7 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(bar_sempty + 8 * a, Cfg::SCHED_CONSUMERS * CG);
     }
     mbar_init(bar_done, 1);
+    mbar_init(bar_skdone, Cfg::EPI_WARPS);
     *abort_flag = 0u;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -255,6 +277,58 @@ __global__ void __launch_bounds__(384, 1)
     }
   };
 
+  // ---- stream-K: worker w owns iterations [w*T/W, (w+1)*T/W) of the T = tiles x
+  // k-blocks iterations, in tile order. A worker's range ends inside at most one
+  // tile (its PARTIAL item, done first so no worker waits before writing) and
+  // starts inside at most one (its LAST item). ----
+  const uint32_t n_workers = gridDim.x / CG;
+  const uint32_t worker = blockIdx.x / CG;
+  const uint64_t total_iters = uint64_t(p.num_tiles) * p.k_blocks;
+  auto sk_start = [&](uint32_t w) -> uint64_t { return total_iters * w / n_workers; };
+  const uint64_t my_begin = sk_start(worker), my_end = sk_start(worker + 1);
+  const bool sk_any = my_begin < my_end;
+  const uint32_t t_first = sk_any ? uint32_t(my_begin / p.k_blocks) : 0u;
+  const uint32_t t_last = sk_any ? uint32_t((my_end - 1) / p.k_blocks) : 0u;
+  const bool last_partial = sk_any && (my_end % p.k_blocks) != 0;
+  const uint32_t n_items = sk_any ? t_last - t_first + 1 : 0u;
+  auto sk_item = [&](uint32_t i, WorkItem& it) -> bool {
+    if (i >= n_items) return false;
+    const uint32_t t = last_partial ? (i == 0 ? t_last : t_first + i - 1) : t_first + i;
+    const uint64_t tb = uint64_t(t) * p.k_blocks, te = tb + p.k_blocks;
+    it.tile = t;
+    it.kb0 = uint32_t((my_begin > tb ? my_begin : tb) - tb);
+    it.kb1 = uint32_t((my_end < te ? my_end : te) - tb);
+    it.kind = it.kb1 < p.k_blocks ? ITEM_PARTIAL : (it.kb0 > 0 ? ITEM_LAST : ITEM_FULL);
+    it.idx = i;
+    return true;
+  };
+  // The worker whose range holds iteration i.
+  auto sk_owner = [&](uint64_t i) -> uint32_t {
+    uint32_t w = uint32_t(i * n_workers / total_iters);
+    while (w + 1 < n_workers && sk_start(w + 1) <= i) ++w;
+    while (w > 0 && sk_start(w) > i) --w;
+    return w;
+  };
+
+  auto first_item = [&](WorkItem& it) -> bool {
+    if constexpr (SCHED == SCHED_STREAMK) {
+      return sk_item(0, it);
+    } else {
+      it = WorkItem{first_tile, 0u, p.k_blocks, ITEM_FULL, 0u};
+      return first_tile < p.num_tiles;
+    }
+  };
+  auto next_item = [&](const WorkItem& cur, WorkItem& nxt) -> bool {
+    if constexpr (SCHED == SCHED_STREAMK) {
+      return sk_item(cur.idx + 1, nxt);
+    } else {
+      uint32_t nt;
+      const bool more = fetch_next(cur.tile, nt);
+      nxt = WorkItem{nt, 0u, p.k_blocks, ITEM_FULL, cur.idx + 1};
+      return more;
+    }
+  };
+
   if (warp == 0) {
     // =============================== TMA producer ===============================
     if (lane == 0) {
@@ -263,17 +337,17 @@ __global__ void __launch_bounds__(384, 1)
       const uint64_t hint = policy_evict_normal();
       const uint32_t leader_full0 = (CG == 2) ? mapa_shared(bar_full, 0) : bar_full;
       if (!p.fault_inject) {
-        uint32_t tile = first_tile;
-        bool more = tile < p.num_tiles;
+        WorkItem cur;
+        bool more = first_item(cur);
         while (more && ok) {
-          uint32_t next;
-          const bool next_more = fetch_next(tile, next);
+          WorkItem nxt;
+          const bool next_more = next_item(cur, nxt);
           uint32_t bm, bn;
-          tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
+          tile_to_bmn(cur.tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
           const int32_t a_row = int32_t((bm * CG + rank) * Cfg::BM);
           // rows of this CTA's share of N-half h: bn*BN + h*256 + rank*B_HALF_ROWS
           const int32_t b_row = int32_t(bn * Cfg::BN + rank * Cfg::B_HALF_ROWS);
-          for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+          for (uint32_t kb = cur.kb0; kb < cur.kb1; ++kb) {
             if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, p.wait_ns, abort_flag)) {
               fail(ST_PRODUCER_EMPTY);
               ok = false;
@@ -311,7 +385,7 @@ __global__ void __launch_bounds__(384, 1)
             if (++stage == S) { stage = 0; phase ^= 1u; }
           }
           if (!ok) break;
-          tile = next;
+          cur = nxt;
           more = next_more;
         }
       }
@@ -338,12 +412,12 @@ __global__ void __launch_bounds__(384, 1)
     if (lane == 0 && rank == 0) {
       uint32_t stage = 0, phase = 0, tile_iter = 0;
       bool ok = true;
-      uint32_t tile = first_tile;
-      bool more = tile < p.num_tiles;
+      WorkItem cur;
+      bool more = first_item(cur);
       while (more && ok) {
-        uint32_t next;
-        const bool next_more = fetch_next(tile, next);
-        for (uint32_t kb = 0; kb < p.k_blocks; ++kb) {
+        WorkItem nxt;
+        const bool next_more = next_item(cur, nxt);
+        for (uint32_t kb = cur.kb0; kb < cur.kb1; ++kb) {
           // TMA completion on the mbarrier makes the stage visible to the MMA; no
           // tcgen05 fence is needed between this wait and the MMAs.
           if (!mbar_wait(bar_full + 8 * stage, phase, p.wait_ns, abort_flag)) {
@@ -356,7 +430,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int h = 0; h < NH; ++h) {
             const uint32_t slot = acc_slot(tile_iter, h);
-            if (kb == 0) {
+            if (kb == cur.kb0) {
               // the slot's previous contents must have been drained by the epilogue
               if (!mbar_wait(bar_tempty + 8 * slot, (acc_use(tile_iter) & 1u) ^ 1u, p.wait_ns,
                              abort_flag)) {
@@ -372,9 +446,9 @@ __global__ void __launch_bounds__(384, 1)
               const uint32_t a_k = a0 + (k / 4) * Cfg::A_ATOM + 32u * (k % 4);
               const uint32_t b_k = b0 + (k / 4) * Cfg::B_ATOM + h * Cfg::B_HALF + 32u * (k % 4);
               umma<CG, Cfg::KIND>(d_tmem, sdesc_k_sw128(a_k), sdesc_k_sw128(b_k), Cfg::IDESC,
-                                  (kb | k) != 0u ? 1u : 0u);
+                                  ((kb - cur.kb0) | k) != 0u ? 1u : 0u);
             }
-            if (kb + 1 == p.k_blocks) {
+            if (kb + 1 == cur.kb1) {
               // Slot h is final once these MMAs complete: signal it now, so with two
               // halves the epilogue drains slot 0 while the last half-1 MMAs run.
               if constexpr (CG == 1) umma_commit<1>(bar_tfull + 8 * slot);
@@ -389,7 +463,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         if (!ok) break;
         ++tile_iter;
-        tile = next;
+        cur = nxt;
         more = next_more;
       }
       // Every MMA this thread issued must retire before TMEM is released.
@@ -445,22 +519,23 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t my_buf = sEpi + (warp - 4) * Cfg::EPI_BUF;
     const uint32_t leader_tempty0 = (CG == 2) ? mapa_shared(bar_tempty, 0) : bar_tempty;
     uint32_t tile_iter = 0;
-    uint32_t tile = first_tile;
-    bool more = tile < p.num_tiles;
+    WorkItem cur;
+    bool more = first_item(cur);
     bool ok = true;
     while (more && ok) {
-      uint32_t next = tile;
+      WorkItem nxt;
       bool next_more;
       if constexpr (SCHED == SCHED_CLC) {
+        uint32_t next = cur.tile;
         bool got = false;
         if (lane == 0) got = clc_next(next);
         next_more = __shfl_sync(0xffffffffu, got ? 1u : 0u, 0) != 0u;
-        next = __shfl_sync(0xffffffffu, next, 0);
+        nxt = WorkItem{__shfl_sync(0xffffffffu, next, 0), 0u, p.k_blocks, ITEM_FULL, cur.idx + 1};
       } else {
-        next_more = fetch_next(tile, next);
+        next_more = next_item(cur, nxt);
       }
       uint32_t bm, bn;
-      tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
+      tile_to_bmn(cur.tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
       const int32_t row0 = int32_t((bm * CG + rank) * Cfg::BM + 32 * q);
 #pragma unroll 1
       for (int h = 0; h < NH; ++h) {
@@ -511,6 +586,67 @@ __global__ void __launch_bounds__(384, 1)
           if constexpr (CG == 1) mbar_arrive(bar_tempty + 8 * slot);
           else mbar_arrive_cluster(leader_tempty0 + 8 * slot);
         }
+        if constexpr (SCHED == SCHED_STREAMK) {
+          // Each thread owns 128 consecutive fp32 values (its row, its columns of the
+          // slot); the workspace stores them thread-major so that every access of a
+          // warp is 512 contiguous bytes: float4 j of warp w4, lane l at (w4*32+j)*32+l.
+          const uint32_t w4 = warp - 4;
+          if (cur.kind == ITEM_PARTIAL) {
+            float4* ws = reinterpret_cast<float4*>(p.sk_work) + size_t(worker * CG + rank) * (Cfg::SK_FLOATS / 4);
+#pragma unroll
+            for (uint32_t j = 0; j < 32; ++j) {
+              const uint32_t f = 4 * j, cc = f / Cfg::EPI_COLS, x = f % Cfg::EPI_COLS;
+              __stcg(ws + (w4 * 32 + j) * 32 + lane,
+                     make_float4(__uint_as_float(r[cc][x]), __uint_as_float(r[cc][x + 1]),
+                                 __uint_as_float(r[cc][x + 2]), __uint_as_float(r[cc][x + 3])));
+            }
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_skdone);
+            if (warp == 4 && lane == 0) {
+              // every epilogue warp wrote its part: publish the partial for this launch
+              if (mbar_wait(bar_skdone, 0, p.wait_ns, abort_flag))
+                st_release_gpu(p.sk_flags + worker * CG + rank, p.sk_epoch);
+              else
+                fail(ST_STREAMK);
+            }
+            continue;  // a partial tile stores no C
+          }
+          if (cur.kind == ITEM_LAST) {
+            // add the partial sums of every worker that owns an earlier part of the tile
+            const uint32_t w_lo = sk_owner(uint64_t(cur.tile) * p.k_blocks);
+            for (uint32_t w2 = w_lo; w2 < worker && ok; ++w2) {
+              if (sk_start(w2) == sk_start(w2 + 1)) continue;  // empty range
+              const uint32_t* flag = p.sk_flags + w2 * CG + rank;
+              uint32_t okf = 1;
+              if (lane == 0) {
+                const uint64_t t0 = globaltimer_ns();
+                while (ld_acquire_gpu(flag) != p.sk_epoch) {
+                  if (*abort_flag || globaltimer_ns() - t0 > p.wait_ns) { okf = 0; break; }
+                  __nanosleep(256);
+                }
+              }
+              okf = __shfl_sync(0xffffffffu, okf, 0);
+              if (!okf) {
+                if (lane == 0) fail(ST_STREAMK);
+                ok = false;
+                break;
+              }
+              const float4* src =
+                  reinterpret_cast<const float4*>(p.sk_work) + size_t(w2 * CG + rank) * (Cfg::SK_FLOATS / 4);
+#pragma unroll
+              for (uint32_t j = 0; j < 32; ++j) {
+                const uint32_t f = 4 * j, cc = f / Cfg::EPI_COLS, x = f % Cfg::EPI_COLS;
+                const float4 v = __ldcg(src + (w4 * 32 + j) * 32 + lane);
+                r[cc][x] = __float_as_uint(__uint_as_float(r[cc][x]) + v.x);
+                r[cc][x + 1] = __float_as_uint(__uint_as_float(r[cc][x + 1]) + v.y);
+                r[cc][x + 2] = __float_as_uint(__uint_as_float(r[cc][x + 2]) + v.z);
+                r[cc][x + 3] = __float_as_uint(__uint_as_float(r[cc][x + 3]) + v.w);
+              }
+            }
+            if (!ok) break;
+          }
+        }
 #pragma unroll
         for (int cc = 0; cc < Cfg::EPI_CHUNKS_PER_WARP; ++cc) {
           uint32_t w[32];
@@ -546,7 +682,7 @@ __global__ void __launch_bounds__(384, 1)
       }
       if (!ok) break;
       ++tile_iter;
-      tile = next;
+      cur = nxt;
       more = next_more;
     }
     if (lane == 0) bulk_wait<0>();

@@ -14,8 +14,9 @@
 // file-scope `static __device__` array of kScratchBytes = 256 bytes, of which a call
 // uses one 32-bit word. Every GPU that loads this library holds the array until
 // the process exits. Requests that would need more scratch than the array holds
-// are rejected with B200_ERR_SCRATCH_LIMIT; the GEMM needs one word for every
-// shape and variant, so today no shape is rejected.
+// are rejected with B200_ERR_SCRATCH_LIMIT: the GEMM needs one word for every
+// shape, but the stream-K variant also needs a 32 MB partial-tile workspace, so an
+// explicit stream-K request is rejected and AUTO never chooses it here.
 //
 // Sharing. All calls on a device share the one array, and it keeps whatever the
 // last call left in it: each call clears its status word (a stream-ordered memset)
@@ -68,8 +69,13 @@ int setup_device(int dev) {
   return B200_OK;
 }
 
-// Scratch a call needs: the kernel's status word, for every shape and variant.
-size_t scratch_bytes_needed(const B200GemmArgs&) { return sizeof(uint32_t); }
+// Scratch a call needs: the kernel's status word; the stream-K schedule also needs
+// its partial-tile workspace (one 128 x 256 fp32 region per CTA), far more than
+// the static array holds, so that variant is refused here (AUTO never picks it).
+size_t scratch_bytes_needed(const B200GemmArgs& a) {
+  if (a.variant == B200_VARIANT_2CTA_STREAMK) return sizeof(uint32_t) + size_t(256) * 128 * 256 * 4;
+  return sizeof(uint32_t);
+}
 
 }  // namespace
 
@@ -87,7 +93,7 @@ extern "C" int b200_gemm_noalloc(const B200GemmArgs* args, void* stream_v, int c
   uint32_t* status = g_scratch_dev[dev];
   // The array keeps the previous call's value: start this call's word at zero.
   if (cudaMemsetAsync(status, 0, sizeof(uint32_t), stream) != cudaSuccess) return B200_ERR_CUDA;
-  rc = b200::gemm_launch_impl(a, stream, g_sms[dev], g_cc_major[dev], status);
+  rc = b200::gemm_launch_impl(a, stream, g_sms[dev], g_cc_major[dev], status, /*allow_workspace=*/false);
   if (rc != B200_OK || !check_status) return rc;
   // Optional synchronous check of this call's status word (no allocation either).
   if (cudaStreamSynchronize(stream) != cudaSuccess) return B200_ERR_CUDA;

@@ -137,6 +137,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// GPU-scope acquire load / release store of a flag in global memory (stream-K
+// partial-tile hand-off between CTAs).
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
 // ---------------------------------------------------------------------------------
 // cluster
 // ---------------------------------------------------------------------------------

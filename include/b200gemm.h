@@ -18,7 +18,10 @@
  *   - Never exits the process (the reference's launchers exit on error,
  *     include/common/errors.h:8-16); every failure is a negative return code.
  *   - Stream-ordered and asynchronous; thread-safe; no allocation on the hot path
- *     (the per-device status word is allocated once, on the first call on a device).
+ *     (the per-device status word is allocated once, on the first call on a device;
+ *     the stream-K workspace, 32 MB, once on the first stream-K call on a device).
+ *   - Stream-K launches on one device share that workspace: launches that overlap
+ *     on the GPU (different streams) must not both use stream-K.
  *   - Device-side waits are bounded: a protocol failure sets the device status
  *     word, which b200_gemm_status() reads back as B200_ERR_DEVICE_TIMEOUT.
  */
@@ -31,7 +34,7 @@
 extern "C" {
 #endif
 
-#define B200GEMM_ABI_VERSION 2
+#define B200GEMM_ABI_VERSION 3
 
 /* element types */
 enum {
@@ -51,8 +54,13 @@ enum {
                                                               (08_persistent persist)  */
   B200_VARIANT_CLC = 4,        /* 1-CTA, cluster-launch-control work stealing
                                                               (08_persistent bn128 dyn)*/
-  B200_VARIANT_2CTA_CLC = 5    /* cta_group::2 pair + cluster-launch-control work
+  B200_VARIANT_2CTA_CLC = 5,   /* cta_group::2 pair + cluster-launch-control work
                                   stealing (the pair form of the persistent kernel) */
+  B200_VARIANT_2CTA_STREAMK = 6 /* cta_group::2 pair, stream-K: every pair takes an equal
+                                  share of the tile x k-block iterations; split tiles are
+                                  summed in a fixed order through a library-owned fp32
+                                  workspace; AUTO takes it only when the tiles would
+                                  leave three quarters of the pairs idle and K is long */
 };
 
 /* return codes */

@@ -68,8 +68,8 @@ int main(void) {{
 
 def test_abi_version_and_strerror(b200):
     L = b200.lib()
-    assert L.b200_gemm_abi_version() == 2
-    for code in (0, -1, -2, -3, -4, -5, -6, -7, -8):
+    assert L.b200_gemm_abi_version() == 3
+    for code in (0, -1, -2, -3, -4, -5, -6, -7, -8, -9):
         assert b200.strerror(code)
     assert "unknown" in b200.strerror(-99)
 
@@ -85,6 +85,10 @@ def test_variant_info(b200):
     for v in ("2cta", "2cta_clc"):
         info = b200.variant_info(v, b200.DT_BF16, tile_n=512)
         assert info["tile_m"] == 256 and info["tile_n"] == 512 and info["max_stages"] == 4
+    info = b200.variant_info("2cta_streamk", b200.DT_F16)
+    assert info["tile_m"] == 256 and info["tile_n"] == 256 and info["max_stages"] == 3
+    with pytest.raises(b200.B200Error):
+        b200.variant_info("2cta_streamk", tile_n=512)  # stream-K uses 256-wide tiles
     with pytest.raises(b200.B200Error):
         b200.variant_info("persistent", tile_n=512)  # 512-wide tiles are pair-only
     with pytest.raises(b200.B200Error):
@@ -169,3 +173,13 @@ def test_product_path_has_no_oracle_or_fallback():
         text = f.read_text()
         assert "import oracle" not in text and "oracle/" not in text.replace("oracle/_ref", ""), f
         assert "torch.matmul" not in text, f
+
+
+def test_noalloc_refuses_streamk_without_touching_the_device(b200):
+    """Stream-K needs a partial-tile workspace that the static array cannot hold;
+    the allocation-free entry point refuses it before any CUDA call."""
+    fn = b200.lib().b200_gemm_noalloc
+    fn.argtypes = [C.POINTER(b200.GemmArgs), C.c_void_p, C.c_int]
+    fn.restype = C.c_int
+    a = _args(b200, variant=b200.VARIANTS["2cta_streamk"])
+    assert fn(C.byref(a), None, 0) == b200.ERR_SCRATCH_LIMIT

@@ -14,6 +14,8 @@ Each case mirrors a CHECK block of the reference or a BASELINE config:
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import numpy as np
 import pytest
 
@@ -24,7 +26,8 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 # "<variant>_w": the same variant with 256x512 pair tiles (tile_n = 512)
-ALL_VARIANTS = ["1cta", "persistent", "clc", "2cta", "2cta_clc", "2cta_w", "2cta_clc_w"]
+ALL_VARIANTS = ["1cta", "persistent", "clc", "2cta", "2cta_clc", "2cta_w", "2cta_clc_w",
+                "2cta_streamk"]
 
 
 def _variant(v):
@@ -85,7 +88,8 @@ def test_ref_check_fp8_512(b200, oracle, variant):
 @pytest.mark.parametrize("group_m", [1, 8])
 @pytest.mark.parametrize("variant,stages", [("persistent", 2), ("persistent", 4), ("clc", 4),
                                             ("2cta", 2), ("2cta", 3), ("2cta_clc", 3),
-                                            ("2cta_w", 2), ("2cta_w", 4), ("2cta_clc_w", 4)])
+                                            ("2cta_w", 2), ("2cta_w", 4), ("2cta_clc_w", 4),
+                                            ("2cta_streamk", 2), ("2cta_streamk", 3)])
 def test_ref_check_fp8_persistent(b200, oracle, shape, group_m, variant, stages):
     """gemm_fp8_persist CHECK: seeds 1001/1002, single- and multi-wave, G in {1,8}."""
     M, N, K = shape
@@ -156,7 +160,8 @@ def test_config4_e4m3_8192_scaled_sampled(b200, oracle):
 
 
 @pytest.mark.parametrize("M,N,K", [(8192, 8192, 1024), (8192, 8192, 4096), (256, 16384, 8192)])
-@pytest.mark.parametrize("variant", ["clc", "persistent", "2cta", "2cta_clc", "2cta_w", "2cta_clc_w"])
+@pytest.mark.parametrize("variant", ["clc", "persistent", "2cta", "2cta_clc", "2cta_w", "2cta_clc_w",
+                                     "2cta_streamk"])
 def test_config5_persistent_sweep(b200, oracle, M, N, K, variant):
     inp = make_inputs(oracle, M, N, K, "e4m3", 907, 908, scaled=True)
     (got,) = _run(b200, inp, variant, "bf16", group_m=8)
@@ -186,7 +191,7 @@ def test_ragged_shapes(b200, oracle, variant, dtype, out, M, N, K):
     assert ok, info
 
 
-@pytest.mark.parametrize("variant", ["persistent", "2cta", "2cta_w"])
+@pytest.mark.parametrize("variant", ["persistent", "2cta", "2cta_w", "2cta_streamk"])
 def test_padded_leading_dims(b200, oracle, variant):
     M, N, K = 384, 512, 320
     inp = make_inputs(oracle, M, N, K, "bf16", 21, 22)
@@ -234,7 +239,7 @@ def test_bounded_wait_reports_timeout_and_context_survives(b200, oracle):
     a, b, _, _ = to_device(inp, torch)
     c = torch.zeros((256, 256), dtype=torch.float16, device="cuda")
     b200.status()  # clear
-    for variant in ("1cta", "2cta", "clc", "2cta_clc", "2cta_w"):
+    for variant in ("1cta", "2cta", "clc", "2cta_clc", "2cta_w", "2cta_streamk"):
         v, tn = _variant(variant)
         b200.gemm(a, b, c, variant=v, tile_n=tn, fault_inject=1, wait_limit_ns=10_000_000)
         rc, bits = b200.status()
@@ -244,6 +249,48 @@ def test_bounded_wait_reports_timeout_and_context_survives(b200, oracle):
     (got,) = _run(b200, inp, "persistent", "f16")
     ok, info = compare(got, reference(oracle, inp), TOL_16)
     assert ok, info
+
+
+# ------------------------------------------------------------------------ stream-K
+@pytest.mark.parametrize("M,N,K,dtype", [
+    (256, 256, 8192, "f16"),      # one tile split over 64 pairs, one k-block each
+    (256, 512, 4096, "bf16"),     # two tiles, each split over ~37 pairs
+    (768, 1280, 2048, "e4m3"),    # 15 tiles, splits of about 3 k-blocks
+    (2048, 2048, 2048, "f16"),    # 64 tiles for 74 pairs (the under-filled wave)
+    (1000, 1000, 1000, "bf16"),   # ragged M/N/K with split tiles
+])
+def test_streamk_split_tiles(b200, oracle, M, N, K, dtype):
+    """Stream-K: tiles whose k-blocks are split over several pairs are summed in fp32
+    in a fixed worker order, so the result is deterministic and matches the oracle."""
+    inp = make_inputs(oracle, M, N, K, dtype, 51, 52, scaled=(dtype == "e4m3"))
+    out = "bf16" if dtype != "f16" else "f16"
+    got = _run(b200, inp, "2cta_streamk", out, reps=3)
+    if M * N * K <= 2048 * 2048 * 2048:
+        ref = reference(oracle, inp)
+        ok, info = compare(got[0], ref, TOL_E4M3 if dtype == "e4m3" else TOL_16)
+        assert ok, info
+    for g in got[1:]:
+        assert np.array_equal(g, got[0])
+
+
+def test_streamk_auto_choice(b200):
+    """AUTO picks stream-K only for a nearly empty pair wave with a long K loop, the
+    static pair schedule whenever pairs need no more waves than 1-CTA tiles, and
+    1-CTA tiles otherwise."""
+    def pick(M, N, K):
+        a = b200.GemmArgs()
+        a.ab_dtype, a.c_dtype = b200.DT_F16, b200.DT_F16
+        a.M, a.N, a.K = M, N, K
+        a.lda, a.ldb, a.ldc = K, K, N
+        a.A, a.B, a.C = 0x10000, 0x20000, 0x30000
+        return b200.lib().b200_gemm_pick_variant(C.byref(a))
+    sk, pair = b200.VARIANTS["2cta_streamk"], b200.VARIANTS["2cta"]
+    assert pick(1024, 1024, 8192) == sk
+    for shape in [(1024, 1024, 4096), (2048, 2048, 2048), (256, 16384, 8192), (8192, 8192, 8192)]:
+        assert pick(*shape) == pair, shape
+    # M = 384 rounds up to two pair rows but three 1-CTA rows: 1-CTA needs fewer waves
+    assert pick(384, 65536, 1024) == b200.VARIANTS["persistent"]
+    assert pick(128, 1024, 1024) == b200.VARIANTS["1cta"]
 
 
 # ------------------------------------------------------------------------ quantiser

@@ -39,6 +39,9 @@ CASES = [
     ("bf16", "bf16", 512, 768, 1024, "2cta", 0, False),
     ("f16", "f16", 300, 520, 200, "persistent", 0, False),
     ("e4m3", "bf16", 1024, 1024, 2048, "2cta", 512, True),
+    # AUTO on a nearly empty pair wave with long K: b200_gemm picks stream-K, the
+    # allocation-free entry point the static pair schedule (no workspace)
+    ("f16", "f16", 1024, 1024, 8192, "auto", 0, False),
 ]
 
 
