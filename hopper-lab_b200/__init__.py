@@ -23,7 +23,7 @@ LIB_PATH = PKG / "lib" / "libb200gemm.so"
 
 DT_F16, DT_BF16, DT_E4M3, DT_F32 = 0, 1, 2, 3
 VARIANTS = {"auto": 0, "1cta": 1, "2cta": 2, "persistent": 3, "clc": 4, "2cta_clc": 5,
-            "2cta_streamk": 6}
+            "2cta_streamk": 6, "2cta_share": 7}
 VARIANT_NAMES = {v: k for k, v in VARIANTS.items()}
 
 OK = 0

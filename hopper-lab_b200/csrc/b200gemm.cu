@@ -187,6 +187,10 @@ int variant_shape(int variant, int tile_n, VariantShape* vs) {
       if (wide) return B200_ERR_INVALID_ARG;
       fill_shape<2, b200::SCHED_STREAMK, 1>(vs);
       break;
+    case B200_VARIANT_2CTA_SHARE:
+      if (tile_n == 256) return B200_ERR_INVALID_ARG;  // built for 256x512 tiles only
+      fill_shape<2, b200::SCHED_SHARE, 2>(vs);
+      break;
     default: return B200_ERR_INVALID_ARG;
   }
   return B200_OK;
@@ -205,6 +209,7 @@ uint32_t variant_smem(const VariantShape& vs, uint32_t stages) {
 // waves of wide tiles. Measured at 8192^3: f16 711 us (512) vs 729 us (256); e4m3
 // equal, so e4m3 keeps 256.
 int pick_tile_n(const B200GemmArgs* a, int variant, int sms) {
+  if (variant == B200_VARIANT_2CTA_SHARE) return 512;
   if (variant != B200_VARIANT_2CTA && variant != B200_VARIANT_2CTA_CLC) return 256;
   if (a->ab_dtype == B200_DT_E4M3 || a->K < 4096) return 256;
   const int64_t wide_tiles = ((a->M + 255) / 256) * ((a->N + 511) / 512);
@@ -284,8 +289,10 @@ int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc
   kp.m_tiles = uint32_t((a.M + vs.tile_m - 1) / vs.tile_m);
   kp.n_tiles = uint32_t((a.N + vs.tile_n - 1) / vs.tile_n);
   const uint64_t tiles = uint64_t(kp.m_tiles) * kp.n_tiles;
-  if (tiles > 0x7fffffffull / 2) return B200_ERR_SHAPE;
+  if (tiles > 0x7fffffffull / 4) return B200_ERR_SHAPE;
   kp.num_tiles = uint32_t(tiles);
+  // B sharing pairs tiles into super-tiles of two block-rows (see tile_coords)
+  if (variant == B200_VARIANT_2CTA_SHARE) kp.num_tiles = 2u * ((kp.m_tiles + 1u) / 2u) * kp.n_tiles;
   kp.k_blocks = uint32_t((a.K + stage_k - 1) / stage_k);
   kp.stages = stages;
   kp.group_m = a.group_m ? uint32_t(a.group_m) : uint32_t(kDefaultGroupM);
@@ -307,6 +314,13 @@ int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc
       break;
     }
     case B200_VARIANT_2CTA_CLC: grid = 2u * kp.num_tiles; break;
+    case B200_VARIANT_2CTA_SHARE: {
+      // an even number of pairs keeps the two pairs of a 4-CTA cluster on the two
+      // halves of one super-tile at every step (the tile count is even as well)
+      const uint32_t pairs = (n_sms / 2) & ~1u;
+      grid = 2u * (kp.num_tiles < pairs ? kp.num_tiles : pairs);
+      break;
+    }
     case B200_VARIANT_2CTA_STREAMK: {
       // every pair must be resident at once (a split tile's last owner waits for
       // the partial sums of the earlier owners), so at most one pair per SM pair
@@ -394,7 +408,7 @@ static int validate(const B200GemmArgs* a) {
     return B200_ERR_INVALID_ARG;
   if (a->c_dtype != B200_DT_F16 && a->c_dtype != B200_DT_BF16 && a->c_dtype != B200_DT_F32)
     return B200_ERR_INVALID_ARG;
-  if (a->variant < B200_VARIANT_AUTO || a->variant > B200_VARIANT_2CTA_STREAMK) return B200_ERR_INVALID_ARG;
+  if (a->variant < B200_VARIANT_AUTO || a->variant > B200_VARIANT_2CTA_SHARE) return B200_ERR_INVALID_ARG;
   if (a->M < 0 || a->N < 0 || a->K < 0) return B200_ERR_SHAPE;
   // TMA coordinates are int32 and the tile counters are uint32.
   const int64_t lim = (int64_t(1) << 31) - 1;

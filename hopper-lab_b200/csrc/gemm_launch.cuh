@@ -38,7 +38,7 @@ cudaError_t launch_gemm(const LaunchPlan& lp) {
   cfg.blockDim = dim3(Cfg::NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = lp.smem;
   cfg.stream = lp.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   if (CG == 2) {
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -46,6 +46,15 @@ cudaError_t launch_gemm(const LaunchPlan& lp) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (SCHED == SCHED_SHARE && lp.grid % 4 == 0) {
+      // two pairs per cluster where a GPC has room, plain pairs elsewhere (on B200:
+      // 33 clusters of 4 and 8 of 2 for a 148-CTA grid)
+      attr[1].id = cudaLaunchAttributePreferredClusterDimension;
+      attr[1].val.preferredClusterDim.x = 4;
+      attr[1].val.preferredClusterDim.y = 1;
+      attr[1].val.preferredClusterDim.z = 1;
+      cfg.numAttrs = 2;
+    }
   }
   if (SCHED == SCHED_STREAMK) {
     // A split tile's last owner waits for the earlier owners' partial sums, so the
@@ -88,6 +97,7 @@ cudaError_t launch_e4m3(int cd, int cg, int sched, int nh, const LaunchPlan& lp)
     } else if (cg == 2 && nh == 2) {                                                     \
       if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 2);               \
       if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 2);                     \
+      if (sched == SCHED_SHARE) B200_DISPATCH_CD(AB, 2, SCHED_SHARE, 2);                 \
     }                                                                                    \
     return cudaErrorNotSupported;                                                        \
   }

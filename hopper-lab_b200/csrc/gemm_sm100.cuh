@@ -19,13 +19,20 @@
 //   gemm_fp8_bn128   (src/08_persistent/gemm_fp8_bn128.cu:73, dynamic queue)
 //                    -> SCHED_CLC: hardware cluster-launch-control work stealing
 //                    replaces the global atomic tile counter
+//   gemm_ws_cluster's shared operand across clusters -> SCHED_SHARE: two CTA pairs in
+//                    one 4-CTA cluster compute vertically adjacent 256 x 512 tiles and
+//                    share B: each CTA loads half of its B rows and copies them into the
+//                    other pair's CTA over DSMEM (a shared::cta -> shared::cluster bulk
+//                    copy, no multicast load), a third less L2 traffic per flop
 //
 // CTA = 384 threads, 12 warps:
 //   warp 0      TMA producer (one lane): A/B k-blocks into an S-stage smem ring
 //               (one 128-byte K atom per stage for 1-CTA tiles, two for pairs)
 //   warp 1      TMEM owner + MMA issuer (one lane of the leader CTA)
-//   warp 2      CLC scheduler (one lane of the leader CTA; SCHED_CLC only)
-//   warp 3      idle
+//   warp 2      CLC scheduler (one lane of the leader CTA; SCHED_CLC only);
+//               SCHED_SHARE: B relay (tells the pair leader a stage's B rows are in)
+//   warp 3      SCHED_SHARE: B forwarder (copies this CTA's B rows to the other pair);
+//               otherwise idle
 //   warps 4-11  epilogue: TMEM -> registers -> (scale, narrow) -> swizzled smem ->
 //               TMA store; warp 4+4e+q drains TMEM lanes 32q..32q+31, columns of half
 //               e of each 256-column slot
@@ -41,7 +48,7 @@
 namespace b200 {
 
 enum : int { DT_F16 = 0, DT_BF16 = 1, DT_E4M3 = 2, DT_F32 = 3 };
-enum : int { SCHED_STATIC = 0, SCHED_CLC = 1, SCHED_STREAMK = 2 };
+enum : int { SCHED_STATIC = 0, SCHED_CLC = 1, SCHED_STREAMK = 2, SCHED_SHARE = 3 };
 
 // Bits OR-ed into the device status word when a bounded wait gives up.
 enum : uint32_t {
@@ -52,6 +59,7 @@ enum : uint32_t {
   ST_SCHED = 1u << 4,
   ST_DRAIN = 1u << 5,
   ST_STREAMK = 1u << 6,
+  ST_SHARE = 1u << 7,
   ST_ABORTED = 1u << 31,
 };
 
@@ -59,7 +67,7 @@ struct KParams {
   uint32_t M, N, K;
   uint32_t m_tiles;    // ceil(M / (128*CG))
   uint32_t n_tiles;    // ceil(N / BN)
-  uint32_t num_tiles;  // m_tiles * n_tiles
+  uint32_t num_tiles;  // m_tiles * n_tiles (SCHED_SHARE: 2 * ceil(m_tiles / 2) * n_tiles)
   uint32_t k_blocks;   // ceil(K / BK)
   uint32_t stages;     // smem ring depth (runtime, ≤ the kernel's maximum)
   uint32_t group_m;    // group-M swizzle width (≥ 1)
@@ -154,6 +162,8 @@ struct GemmCfg {
   }
   static_assert(NH == 1 || (NH == 2 && CG == 2), "512-wide tiles are built for CTA pairs");
   static_assert(SCHED != SCHED_STREAMK || NH == 1, "stream-K uses 256-wide tiles");
+  static_assert(SCHED != SCHED_SHARE || (CG == 2 && NH == 2 && ATOMS == 1),
+                "B sharing is built for 256 x 512 pair tiles (one contiguous B box per half)");
   // stream-K partial of one CTA: 128 rows x 256 fp32 columns
   static constexpr uint32_t SK_FLOATS = BM * MMA_N;
   static_assert(MAX_STAGES <= 8, "the barrier block holds 8 ring stages");
@@ -191,14 +201,30 @@ __global__ void __launch_bounds__(384, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 304);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(bar_ptr + 308);
   const uint32_t bar_skdone = sBar + 320;               // stream-K: partial written
+  const uint32_t bar_own = sBar + 336;                  // SCHED_SHARE: own B box landed [8]
+  const uint32_t bar_fwd = sBar + 400;                  // SCHED_SHARE: forwarded B box in [8]
 
   const uint32_t warp = warp_id(), lane = lane_id();
-  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+  // Cluster rank; in-pair rank (0 = the pair's MMA leader); the leader's cluster rank.
+  // SCHED_SHARE launches prefer 4-CTA clusters (two pairs, which share B) and fall
+  // back to plain pairs where 4 CTAs do not fit in a GPC.
+  const uint32_t crank = (CG == 2) ? cluster_ctarank() : 0u;
+  const uint32_t rank = crank & 1u;
+  const uint32_t lead = crank & ~1u;
+  bool share = false;
+  if constexpr (SCHED == SCHED_SHARE) share = cluster_nctarank() == 4u;
+  const uint32_t pair_mask = 3u << lead;              // commit mask: this pair
+  const uint32_t empty_mask = share ? 0xFu : pair_mask; // stage release: both pairs
+  const uint32_t xpeer = crank ^ 2u;                  // same in-pair rank, other pair
 
   if (warp == 0 && lane == 0) {
     for (uint32_t s = 0; s < S; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, 1);
+      // sharing: the leader's arm (A bytes) + one relay arrive per CTA of the pair
+      mbar_init(bar_full + 8 * s, share ? 3 : 1);
+      // sharing: a stage is reused only once both pairs' MMAs have read it
+      mbar_init(bar_empty + 8 * s, share ? 2 : 1);
+      mbar_init(bar_own + 8 * s, 1);
+      mbar_init(bar_fwd + 8 * s, 1);
     }
     for (uint32_t a = 0; a < 2; ++a) {
       mbar_init(bar_tfull + 8 * a, 1);
@@ -239,13 +265,31 @@ __global__ void __launch_bounds__(384, 1)
   auto acc_slot = [](uint32_t it, int h) -> uint32_t { return NH == 1 ? (it & 1u) : uint32_t(h); };
   auto acc_use = [](uint32_t it) -> uint32_t { return NH == 1 ? (it >> 1) : it; };
 
+  // ---- tile id -> (block-row, block-col) ----
+  // SCHED_SHARE: tiles 2u and 2u+1 are the upper and lower halves of super-tile u (two
+  // vertically adjacent pair tiles with the same columns), super-tiles in group-M order
+  // with groups of G/2 super-rows. The static stride is even, so the two pairs of a
+  // 4-CTA cluster (pair slots 2c, 2c+1) always hold the two halves of one super-tile.
+  // A lower half past the last block-row (odd row count) is computed on zero-filled A
+  // and not stored.
+  auto tile_coords = [&](uint32_t tile, uint32_t& bm, uint32_t& bn) {
+    if constexpr (SCHED == SCHED_SHARE) {
+      uint32_t sm;
+      const uint32_t g2 = p.group_m > 1u ? p.group_m / 2u : 1u;
+      tile_to_bmn(tile >> 1, (p.m_tiles + 1u) / 2u, p.n_tiles, g2, sm, bn);
+      bm = 2u * sm + (tile & 1u);
+    } else {
+      tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
+    }
+  };
+
   // ---- tile sequence shared by every role ----
   // SCHED_STATIC: cluster c takes tiles c, c + G, c + 2G, ... (G = clusters in grid)
   // SCHED_CLC   : tile = this cluster's own index first, then whatever the
   //               leader's try_cancel returns (forwarded to the peer)
   const uint32_t first_tile = blockIdx.x / CG;
   const uint32_t tile_stride = gridDim.x / CG;
-  const uint32_t leader_sempty0 = (CG == 2) ? mapa_shared(bar_sempty, 0) : bar_sempty;
+  const uint32_t leader_sempty0 = (CG == 2) ? mapa_shared(bar_sempty, lead) : bar_sempty;
 
   // Consumer side of the CLC ring: wait for slot, decode, release it to the leader.
   // Returns false when the grid is exhausted (tile unchanged) or on abort.
@@ -335,7 +379,7 @@ __global__ void __launch_bounds__(384, 1)
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
       const uint64_t hint = policy_evict_normal();
-      const uint32_t leader_full0 = (CG == 2) ? mapa_shared(bar_full, 0) : bar_full;
+      const uint32_t leader_full0 = (CG == 2) ? mapa_shared(bar_full, lead) : bar_full;
       if (!p.fault_inject) {
         WorkItem cur;
         bool more = first_item(cur);
@@ -343,7 +387,7 @@ __global__ void __launch_bounds__(384, 1)
           WorkItem nxt;
           const bool next_more = next_item(cur, nxt);
           uint32_t bm, bn;
-          tile_to_bmn(cur.tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
+          tile_coords(cur.tile, bm, bn);
           const int32_t a_row = int32_t((bm * CG + rank) * Cfg::BM);
           // rows of this CTA's share of N-half h: bn*BN + h*256 + rank*B_HALF_ROWS
           const int32_t b_row = int32_t(bn * Cfg::BN + rank * Cfg::B_HALF_ROWS);
@@ -365,6 +409,20 @@ __global__ void __launch_bounds__(384, 1)
                   tma_load_2d(sB + stage * Cfg::B_STAGE + at * Cfg::B_ATOM + h * Cfg::B_HALF, &tmB, x,
                               b_row + h * Cfg::MMA_N, bar_full + 8 * stage, hint);
               }
+            } else if (share) {
+              // A as in a plain pair (both CTAs credit the leader, which arms A only).
+              // B: this CTA loads N-half `crank >> 1` of its rows into its own-box
+              // barrier; the forwarder copies it to the other pair and the other
+              // pair's copy of the second half lands on the forwarded-box barrier.
+              // The relay then tells the leader that this CTA's B is complete.
+              if (rank == 0) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * Cfg::A_STAGE);
+              mbar_arrive_expect_tx(bar_own + 8 * stage, Cfg::B_HALF);
+              mbar_arrive_expect_tx(bar_fwd + 8 * stage, Cfg::B_HALF);
+              const uint32_t lf = leader_full0 + 8 * stage;
+              const int h = int(crank >> 1);
+              tma_load_2d_pair(sA + stage * Cfg::A_STAGE, &tmA, kx, a_row, lf, hint);
+              tma_load_2d(sB + stage * Cfg::B_STAGE + h * Cfg::B_HALF, &tmB, kx, b_row + h * Cfg::MMA_N,
+                          bar_own + 8 * stage, hint);
             } else {
               // Both CTAs' bytes are credited to the leader's full barrier; only the
               // leader arms it (a peer credit that lands first leaves the tx count
@@ -452,13 +510,14 @@ __global__ void __launch_bounds__(384, 1)
               // Slot h is final once these MMAs complete: signal it now, so with two
               // halves the epilogue drains slot 0 while the last half-1 MMAs run.
               if constexpr (CG == 1) umma_commit<1>(bar_tfull + 8 * slot);
-              else umma_commit_pair(bar_tfull + 8 * slot, 0x3);
+              else umma_commit_pair(bar_tfull + 8 * slot, uint16_t(pair_mask));
             }
           }
           if (!ok) break;
-          // frees this stage in both CTAs once the MMAs above have read it
+          // frees this stage in both CTAs once the MMAs above have read it (sharing:
+          // in all four CTAs, whose empty barriers wait for both pairs' commits)
           if constexpr (CG == 1) umma_commit<1>(bar_empty + 8 * stage);
-          else umma_commit_pair(bar_empty + 8 * stage, 0x3);
+          else umma_commit_pair(bar_empty + 8 * stage, uint16_t(empty_mask));
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
@@ -507,6 +566,72 @@ __global__ void __launch_bounds__(384, 1)
           if (++slot == Cfg::CLC_SLOTS) { slot = 0; ph ^= 1u; }
         }
       }
+    } else if constexpr (SCHED == SCHED_SHARE) {
+      // ================================ B relay ================================
+      // Once this CTA holds both B boxes of a stage (its own load and the other
+      // pair's copy), tell the pair leader, whose full barrier counts one relay
+      // arrive per CTA of the pair on top of the A bytes.
+      if (lane == 0 && share) {
+        const uint32_t leader_full0 = mapa_shared(bar_full, lead);
+        uint32_t stage = 0, phase = 0;
+        bool ok = true;
+        WorkItem cur;
+        bool more = first_item(cur);
+        while (more && ok) {
+          WorkItem nxt;
+          const bool next_more = next_item(cur, nxt);
+          for (uint32_t kb = cur.kb0; kb < cur.kb1; ++kb) {
+            if (!mbar_wait(bar_own + 8 * stage, phase, p.wait_ns, abort_flag) ||
+                !mbar_wait<true>(bar_fwd + 8 * stage, phase, p.wait_ns, abort_flag)) {
+              fail(ST_SHARE);
+              ok = false;
+              break;
+            }
+            mbar_arrive_cluster(leader_full0 + 8 * stage);
+            if (++stage == S) { stage = 0; phase ^= 1u; }
+          }
+          cur = nxt;
+          more = next_more;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 3) {
+    // ============================== B forwarder ==============================
+    // SCHED_SHARE in a 4-CTA cluster: copy this CTA's own B box of every stage into
+    // the same place of the other pair's CTA with the same in-pair rank. That CTA's
+    // stage is free: this CTA's own load was issued only after its empty barrier saw
+    // both pairs' MMAs release the stage.
+    if constexpr (SCHED == SCHED_SHARE) {
+      if (lane == 0 && share) {
+        const uint32_t h = crank >> 1;
+        uint32_t stage = 0, phase = 0;
+        bool ok = true;
+        WorkItem cur;
+        bool more = first_item(cur);
+        while (more && ok) {
+          WorkItem nxt;
+          const bool next_more = next_item(cur, nxt);
+          for (uint32_t kb = cur.kb0; kb < cur.kb1; ++kb) {
+            if (!mbar_wait(bar_own + 8 * stage, phase, p.wait_ns, abort_flag)) {
+              fail(ST_SHARE);
+              ok = false;
+              break;
+            }
+            const uint32_t box = sB + stage * Cfg::B_STAGE + h * Cfg::B_HALF;
+            bulk_copy_s2c(mapa_shared(box, xpeer), box, Cfg::B_HALF, mapa_shared(bar_fwd + 8 * stage, xpeer));
+            if (++stage == S) { stage = 0; phase ^= 1u; }
+          }
+          cur = nxt;
+          more = next_more;
+        }
+        if (!ok || *abort_flag) {
+          // give copies still reading this CTA's shared memory a fixed 50 us
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 50000ull) {
+          }
+        }
+      }
     }
     __syncwarp();
   } else if (warp >= 4) {
@@ -517,7 +642,7 @@ __global__ void __launch_bounds__(384, 1)
     if (p.scale_a) scale *= __ldg(p.scale_a);
     if (p.scale_b) scale *= __ldg(p.scale_b);
     const uint32_t my_buf = sEpi + (warp - 4) * Cfg::EPI_BUF;
-    const uint32_t leader_tempty0 = (CG == 2) ? mapa_shared(bar_tempty, 0) : bar_tempty;
+    const uint32_t leader_tempty0 = (CG == 2) ? mapa_shared(bar_tempty, lead) : bar_tempty;
     uint32_t tile_iter = 0;
     WorkItem cur;
     bool more = first_item(cur);
@@ -535,7 +660,7 @@ __global__ void __launch_bounds__(384, 1)
         next_more = next_item(cur, nxt);
       }
       uint32_t bm, bn;
-      tile_to_bmn(cur.tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
+      tile_coords(cur.tile, bm, bn);
       const int32_t row0 = int32_t((bm * CG + rank) * Cfg::BM + 32 * q);
 #pragma unroll 1
       for (int h = 0; h < NH; ++h) {

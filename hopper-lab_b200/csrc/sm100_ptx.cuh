@@ -157,6 +157,12 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   return r;
 }
 
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
 // Translate a local shared::cta address into the shared::cluster address of the
 // same offset in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
@@ -215,6 +221,19 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, uint32_t src,
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(m),
                "r"(x), "r"(y), "r"(src)
                : "memory");
+}
+
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this
+// CTA's shared memory into another CTA's shared memory of the cluster; completion is
+// counted on `mbar_cluster`, a barrier in the destination CTA. A plain point-to-point
+// copy between SMs: no global memory is read and nothing is multicast.
+__device__ __forceinline__ void bulk_copy_s2c(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
+                                              uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(src), "r"(bytes), "r"(mbar_cluster)
+      : "memory");
 }
 
 __device__ __forceinline__ void bulk_commit() {

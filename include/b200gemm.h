@@ -60,7 +60,14 @@ enum {
                                   share of the tile x k-block iterations; split tiles are
                                   summed in a fixed order through a library-owned fp32
                                   workspace; AUTO takes it only when the tiles would
-                                  leave three quarters of the pairs idle and K is long */
+                                  leave three quarters of the pairs idle and K is long */,
+  B200_VARIANT_2CTA_SHARE = 7  /* two cta_group::2 pairs per 4-CTA cluster (2-CTA where a
+                                  GPC has no room for 4) computing vertically adjacent
+                                  256x512 tiles; each CTA loads half of its B rows and
+                                  copies them to the other pair over DSMEM (no
+                                  multicast load): a third less L2 traffic per flop,
+                                  but slower than 2CTA on B200 (SM-to-SM copies stream
+                                  at ~32 GB/s per SM); never picked by AUTO          */
 };
 
 /* return codes */

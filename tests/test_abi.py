@@ -89,6 +89,10 @@ def test_variant_info(b200):
     assert info["tile_m"] == 256 and info["tile_n"] == 256 and info["max_stages"] == 3
     with pytest.raises(b200.B200Error):
         b200.variant_info("2cta_streamk", tile_n=512)  # stream-K uses 256-wide tiles
+    info = b200.variant_info("2cta_share", b200.DT_F16)
+    assert info["tile_m"] == 256 and info["tile_n"] == 512 and info["max_stages"] == 4
+    with pytest.raises(b200.B200Error):
+        b200.variant_info("2cta_share", tile_n=256)  # B sharing uses 256x512 tiles
     with pytest.raises(b200.B200Error):
         b200.variant_info("persistent", tile_n=512)  # 512-wide tiles are pair-only
     with pytest.raises(b200.B200Error):
@@ -168,7 +172,8 @@ def test_product_path_has_no_oracle_or_fallback():
     """The library and its Python mirror never reach into oracle/ or a CPU GEMM."""
     pkg = ROOT / "hopper-lab_b200"
     product = [f for f in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cuh"))
-               if f.name != "profile_case.py"]  # the profiling driver times cuBLAS on purpose
+               # the profiling and power drivers time cuBLAS on purpose, as the reference column
+               if f.name not in ("profile_case.py", "power_case.py")]
     for f in product:
         text = f.read_text()
         assert "import oracle" not in text and "oracle/" not in text.replace("oracle/_ref", ""), f

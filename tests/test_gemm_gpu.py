@@ -27,7 +27,7 @@ pytestmark = pytest.mark.gpu
 
 # "<variant>_w": the same variant with 256x512 pair tiles (tile_n = 512)
 ALL_VARIANTS = ["1cta", "persistent", "clc", "2cta", "2cta_clc", "2cta_w", "2cta_clc_w",
-                "2cta_streamk"]
+                "2cta_streamk", "2cta_share"]
 
 
 def _variant(v):
@@ -89,7 +89,8 @@ def test_ref_check_fp8_512(b200, oracle, variant):
 @pytest.mark.parametrize("variant,stages", [("persistent", 2), ("persistent", 4), ("clc", 4),
                                             ("2cta", 2), ("2cta", 3), ("2cta_clc", 3),
                                             ("2cta_w", 2), ("2cta_w", 4), ("2cta_clc_w", 4),
-                                            ("2cta_streamk", 2), ("2cta_streamk", 3)])
+                                            ("2cta_streamk", 2), ("2cta_streamk", 3),
+                                            ("2cta_share", 2), ("2cta_share", 4)])
 def test_ref_check_fp8_persistent(b200, oracle, shape, group_m, variant, stages):
     """gemm_fp8_persist CHECK: seeds 1001/1002, single- and multi-wave, G in {1,8}."""
     M, N, K = shape
@@ -129,7 +130,7 @@ def test_config2_fp16_2048(b200, oracle, variant):
     assert ok, info
 
 
-@pytest.mark.parametrize("variant", ["2cta", "persistent", "2cta_w"])
+@pytest.mark.parametrize("variant", ["2cta", "persistent", "2cta_w", "2cta_share"])
 def test_config3_bf16_8192_sampled(b200, oracle, variant):
     """bf16 8192^3, normal(0,1)*0.1 seeds 605/606; seeded row bands vs the oracle."""
     inp = make_inputs(oracle, 8192, 8192, 8192, "bf16", 605, 606, dist="normal")
@@ -161,7 +162,7 @@ def test_config4_e4m3_8192_scaled_sampled(b200, oracle):
 
 @pytest.mark.parametrize("M,N,K", [(8192, 8192, 1024), (8192, 8192, 4096), (256, 16384, 8192)])
 @pytest.mark.parametrize("variant", ["clc", "persistent", "2cta", "2cta_clc", "2cta_w", "2cta_clc_w",
-                                     "2cta_streamk"])
+                                     "2cta_streamk", "2cta_share"])
 def test_config5_persistent_sweep(b200, oracle, M, N, K, variant):
     inp = make_inputs(oracle, M, N, K, "e4m3", 907, 908, scaled=True)
     (got,) = _run(b200, inp, variant, "bf16", group_m=8)
@@ -191,7 +192,7 @@ def test_ragged_shapes(b200, oracle, variant, dtype, out, M, N, K):
     assert ok, info
 
 
-@pytest.mark.parametrize("variant", ["persistent", "2cta", "2cta_w", "2cta_streamk"])
+@pytest.mark.parametrize("variant", ["persistent", "2cta", "2cta_w", "2cta_streamk", "2cta_share"])
 def test_padded_leading_dims(b200, oracle, variant):
     M, N, K = 384, 512, 320
     inp = make_inputs(oracle, M, N, K, "bf16", 21, 22)
@@ -239,7 +240,7 @@ def test_bounded_wait_reports_timeout_and_context_survives(b200, oracle):
     a, b, _, _ = to_device(inp, torch)
     c = torch.zeros((256, 256), dtype=torch.float16, device="cuda")
     b200.status()  # clear
-    for variant in ("1cta", "2cta", "clc", "2cta_clc", "2cta_w", "2cta_streamk"):
+    for variant in ("1cta", "2cta", "clc", "2cta_clc", "2cta_w", "2cta_streamk", "2cta_share"):
         v, tn = _variant(variant)
         b200.gemm(a, b, c, variant=v, tile_n=tn, fault_inject=1, wait_limit_ns=10_000_000)
         rc, bits = b200.status()
@@ -291,6 +292,32 @@ def test_streamk_auto_choice(b200):
     # M = 384 rounds up to two pair rows but three 1-CTA rows: 1-CTA needs fewer waves
     assert pick(384, 65536, 1024) == b200.VARIANTS["persistent"]
     assert pick(128, 1024, 1024) == b200.VARIANTS["1cta"]
+
+
+# ------------------------------------------------------------------ shared-B clusters
+@pytest.mark.parametrize("M,N,K,dtype", [
+    (768, 1536, 512, "f16"),      # three block-rows: the last super-tile's lower half is empty
+    (8192, 2048, 1024, "bf16"),   # 74 pairs: 4-CTA clusters and the 2-CTA fallback together
+    (4352, 4608, 640, "e4m3"),    # 17 block-rows, 9 tile columns, ragged K stages
+])
+def test_share_b_clusters(b200, oracle, M, N, K, dtype):
+    """Two pairs per cluster share B over DSMEM: every block-row (upper and lower halves
+    of the super-tiles, and plain pairs where no 4-CTA cluster fits) matches the oracle,
+    and repeated launches are bit-identical."""
+    inp = make_inputs(oracle, M, N, K, dtype, 61, 62, scaled=(dtype == "e4m3"))
+    out = "f16" if dtype == "f16" else "bf16"
+    got = _run(b200, inp, "2cta_share", out, reps=2, group_m=8)
+    tol = TOL_E4M3 if dtype == "e4m3" else TOL_16
+    if M * N * K <= 768 * 1536 * 512:
+        ok, info = compare(got[0], reference(oracle, inp), tol)
+        assert ok, info
+    else:
+        # one 32-row band in every 256-row block-row
+        for r0 in range(0, M, 256):
+            r1 = min(r0 + 32, M)
+            ok, info = compare(got[0][r0:r1], reference(oracle, inp, rows=(r0, r1)), tol)
+            assert ok, (r0, info)
+    assert np.array_equal(got[0], got[1])
 
 
 # ------------------------------------------------------------------------ quantiser
