@@ -206,12 +206,13 @@ uint32_t variant_smem(const VariantShape& vs, uint32_t stages) {
 // 256x512 tile cuts operand traffic by a quarter (less power, so a
 // higher clock under the power cap) but its accumulator is single-buffered, so it
 // only pays when the main loop is long (K >= 4096) and there are at least two
-// waves of wide tiles. Measured at 8192^3: f16 711 us (512) vs 729 us (256); e4m3
-// equal, so e4m3 keeps 256.
+// waves of wide tiles. Measured, one launch at 8192^3: f16 711 us (512) vs 729 us
+// (256), e4m3 equal; sustained under the power cap: f16 1282 vs 1217 TFLOPS, e4m3
+// 2489 vs 2464 (8192^3) and 2497 vs 2438 (16384^3), with less energy per GEMM.
 int pick_tile_n(const B200GemmArgs* a, int variant, int sms) {
   if (variant == B200_VARIANT_2CTA_SHARE) return 512;
   if (variant != B200_VARIANT_2CTA && variant != B200_VARIANT_2CTA_CLC) return 256;
-  if (a->ab_dtype == B200_DT_E4M3 || a->K < 4096) return 256;
+  if (a->K < 4096) return 256;
   const int64_t wide_tiles = ((a->M + 255) / 256) * ((a->N + 511) / 512);
   return wide_tiles >= sms ? 512 : 256;
 }
