@@ -158,6 +158,12 @@ def timed_loop(torch, fn, steps: int, warmup: int, stream):
     return t0.elapsed_time(t1), per
 
 
+def launch_stats(per):
+    """Min / median / mean of the per-launch event times of one rank (ms)."""
+    return {"min": round(min(per), 5), "median": round(statistics.median(per), 5),
+            "mean": round(statistics.fmean(per), 5)}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -328,11 +334,13 @@ def run_ours(args):
                 "frac": round(fp8_kernel / (2 * peak), 4) if peak else None,
                 "peak_kind": "2 x measured bf16 (e4m3 dense rate is twice bf16)",
                 "config": "e4m3 8192^3, per-tensor scales amax/448, bf16 C",
-                "traffic": profile_traffic("e4m3_8192"), "clocks": clk8.summary()},
+                "traffic": profile_traffic("e4m3_8192"), "clocks": clk8.summary(),
+                "launch_ms": launch_stats(per8)},
         "cublaslt": cublas,
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOPS",
                 "h2d_bytes_per_step": 2 * M * K * 2, "d2h_bytes_per_step": M * N * 2,
                 "steps": e2e_steps, "path": "pinned host A,B -> device -> b200_gemm -> pinned host C"},
+        "launch_ms": launch_stats(per),
         "gpu_launches": args.steps,
         "gpu_launches_note": "fp16 timed region; the fp8 region adds the same count",
         "clocks": clk.summary(),
