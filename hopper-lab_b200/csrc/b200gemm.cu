@@ -236,6 +236,11 @@ int pick_variant(const B200GemmArgs* a, int sms, bool allow_workspace) {
       const int64_t stage_k = (a->ab_dtype == B200_DT_E4M3) ? 256 : 128;
       if ((a->K + stage_k - 1) / stage_k >= 48) return B200_VARIANT_2CTA_STREAMK;
     }
+    // More than one wave: the persistent pairs take their next tiles from
+    // cluster-launch-control work stealing (even with the static order's speed:
+    // 8192^3 sustained f16 1302 vs 1293 TFLOPS, e4m3 2597 vs 2580, and it adapts to
+    // SMs that run slower or are shared). One wave needs no scheduler at all.
+    if (pair_tiles > pairs) return B200_VARIANT_2CTA_CLC;
     return B200_VARIANT_2CTA;
   }
   return cta_tiles > sms ? B200_VARIANT_PERSISTENT : B200_VARIANT_1CTA;

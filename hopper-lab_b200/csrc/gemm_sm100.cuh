@@ -145,7 +145,7 @@ struct GemmCfg {
   static constexpr uint32_t IDESC =
       idesc_f32acc(AB == DT_BF16 ? 1u : 0u, AB == DT_BF16 ? 1u : 0u, MMA_M, MMA_N);
   static constexpr uint32_t MAX_SMEM = 232448;         // 227 KB opt-in per CTA
-  static constexpr uint32_t BAR_BYTES = 512;
+  static constexpr uint32_t BAR_BYTES = 576;
   // CLC response ring depth: the scheduler may run this many tiles ahead of the
   // slowest consumer (at small K a tile is only a few stages long, and a
   // try_cancel round trip plus the pair forwarding must fit in the lead).
@@ -167,6 +167,7 @@ struct GemmCfg {
   // stream-K partial of one CTA: 128 rows x 256 fp32 columns
   static constexpr uint32_t SK_FLOATS = BM * MMA_N;
   static_assert(MAX_STAGES <= 8, "the barrier block holds 8 ring stages");
+  static_assert(CLC_SLOTS <= 8, "the barrier block holds 8 CLC response slots");
 };
 
 template <int AB, int CD, int CG, int SCHED, int NH>
@@ -188,21 +189,22 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t sEpi = base + S * Cfg::STAGE;
   const uint32_t sBar = sEpi + Cfg::EPI_BYTES;
   uint8_t* bar_ptr = base_ptr + (sBar - base);
-  // 8-byte barriers: full[8], empty[8], tfull[2], tempty[2], sfull[4], sempty[4], done;
-  // then the CLC responses (4 × 16 B), the TMEM base address and the abort flag
+  // 8-byte barriers and words: full[8], empty[8], tfull[2], tempty[2], done, skdone,
+  // the TMEM base address, the abort flag; then the CLC ring (sfull, sempty, 16-byte
+  // responses) and the B-sharing barriers (own, fwd)
   const uint32_t bar_full = sBar;
   const uint32_t bar_empty = sBar + 64;
   const uint32_t bar_tfull = sBar + 128;
   const uint32_t bar_tempty = sBar + 144;
-  const uint32_t bar_sfull = sBar + 160;
-  const uint32_t bar_sempty = sBar + 192;
-  const uint32_t bar_done = sBar + 224;
-  const uint32_t clc_resp = sBar + 240;                 // 4 × 16 B
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 304);
-  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(bar_ptr + 308);
-  const uint32_t bar_skdone = sBar + 320;               // stream-K: partial written
-  const uint32_t bar_own = sBar + 336;                  // SCHED_SHARE: own B box landed [8]
-  const uint32_t bar_fwd = sBar + 400;                  // SCHED_SHARE: forwarded B box in [8]
+  const uint32_t bar_done = sBar + 160;
+  const uint32_t bar_skdone = sBar + 168;               // stream-K: partial written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 176);
+  volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(bar_ptr + 180);
+  const uint32_t bar_sfull = sBar + 192;                // CLC_SLOTS (≤ 8)
+  const uint32_t bar_sempty = sBar + 256;               // CLC_SLOTS
+  const uint32_t clc_resp = sBar + 320;                 // CLC_SLOTS × 16 B
+  const uint32_t bar_own = sBar + 448;                  // SCHED_SHARE: own B box landed [8]
+  const uint32_t bar_fwd = sBar + 512;                  // SCHED_SHARE: forwarded B box in [8]
 
   const uint32_t warp = warp_id(), lane = lane_id();
   // Cluster rank; in-pair rank (0 = the pair's MMA leader); the leader's cluster rank.
@@ -302,7 +304,7 @@ __global__ void __launch_bounds__(384, 1)
     uint32_t x = 0;
     const bool got = clc_decode(clc_resp + 16 * sched_slot, x);
     if constexpr (CG == 1) mbar_arrive(bar_sempty + 8 * sched_slot);
-    else mbar_arrive_cluster(leader_sempty0 + 8 * sched_slot);
+    else mbar_arrive_cluster_relaxed(leader_sempty0 + 8 * sched_slot);  // slot read: relaxed
     if (++sched_slot == Cfg::CLC_SLOTS) { sched_slot = 0; sched_phase ^= 1u; }
     if (got) tile = x / CG;
     return got;
@@ -709,7 +711,7 @@ __global__ void __launch_bounds__(384, 1)
         __syncwarp();
         if (lane == 0) {
           if constexpr (CG == 1) mbar_arrive(bar_tempty + 8 * slot);
-          else mbar_arrive_cluster(leader_tempty0 + 8 * slot);
+          else mbar_arrive_cluster_relaxed(leader_tempty0 + 8 * slot);  // TMEM read: relaxed
         }
         if constexpr (SCHED == SCHED_STREAMK) {
           // Each thread owns 128 consecutive fp32 values (its row, its columns of the

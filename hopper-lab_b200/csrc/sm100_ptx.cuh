@@ -66,6 +66,18 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
                : "memory");
 }
 
+// Relaxed remote arrive, for "I have finished READING this" signals (a consumed CLC
+// response slot, a drained TMEM accumulator): the reads are complete before the
+// arrive executes (their values are in registers: the response was decoded, and
+// tcgen05.wait::ld returned), so no release ordering is needed. A release.cluster
+// arrive also waits for this thread's earlier memory operations (e.g. the epilogue's
+// in-flight TMA stores) to become visible cluster-wide, which measured ~1 us per
+// arrive and stalled the pair kernels' MMA and scheduler.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
   asm volatile(

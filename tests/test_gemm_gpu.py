@@ -275,9 +275,9 @@ def test_streamk_split_tiles(b200, oracle, M, N, K, dtype):
 
 
 def test_streamk_auto_choice(b200):
-    """AUTO picks stream-K only for a nearly empty pair wave with a long K loop, the
-    static pair schedule whenever pairs need no more waves than 1-CTA tiles, and
-    1-CTA tiles otherwise."""
+    """AUTO picks stream-K only for a nearly empty pair wave with a long K loop; pairs
+    whenever they need no more waves than 1-CTA tiles (static for one wave, CLC work
+    stealing for more); 1-CTA tiles otherwise."""
     def pick(M, N, K):
         a = b200.GemmArgs()
         a.ab_dtype, a.c_dtype = b200.DT_F16, b200.DT_F16
@@ -285,10 +285,12 @@ def test_streamk_auto_choice(b200):
         a.lda, a.ldb, a.ldc = K, K, N
         a.A, a.B, a.C = 0x10000, 0x20000, 0x30000
         return b200.lib().b200_gemm_pick_variant(C.byref(a))
-    sk, pair = b200.VARIANTS["2cta_streamk"], b200.VARIANTS["2cta"]
+    sk, pair, clc = b200.VARIANTS["2cta_streamk"], b200.VARIANTS["2cta"], b200.VARIANTS["2cta_clc"]
     assert pick(1024, 1024, 8192) == sk
-    for shape in [(1024, 1024, 4096), (2048, 2048, 2048), (256, 16384, 8192), (8192, 8192, 8192)]:
-        assert pick(*shape) == pair, shape
+    for shape in [(1024, 1024, 4096), (2048, 2048, 2048), (256, 16384, 8192)]:
+        assert pick(*shape) == pair, shape  # one wave of pair tiles: static
+    for shape in [(8192, 8192, 8192), (4096, 4096, 4096), (8192, 8192, 1024)]:
+        assert pick(*shape) == clc, shape  # several waves: CLC work stealing
     # M = 384 rounds up to two pair rows but three 1-CTA rows: 1-CTA needs fewer waves
     assert pick(384, 65536, 1024) == b200.VARIANTS["persistent"]
     assert pick(128, 1024, 1024) == b200.VARIANTS["1cta"]
