@@ -255,6 +255,10 @@ __global__ void __launch_bounds__(384, 1)
   if constexpr (CG == 2) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The set-up above touches no global memory, so with programmatic dependent launch
+  // it overlaps the previous kernel's tail; every global access comes after this wait.
+  griddep_wait();
+  griddep_launch_dependents();
 
   auto fail = [&](uint32_t code) {
     *abort_flag = 1u;

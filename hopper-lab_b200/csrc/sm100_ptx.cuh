@@ -66,6 +66,16 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
                : "memory");
 }
 
+// Programmatic dependent launch: wait until every prerequisite grid of the stream has
+// completed and its memory is visible (before this kernel's first global access), and
+// allow the next kernel of the stream to be scheduled once all CTAs of this grid ran
+// launch_dependents (its CTAs then do their set-up on SMs this grid leaves free and
+// wait in their own griddepcontrol.wait).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Relaxed remote arrive, for "I have finished READING this" signals (a consumed CLC
 // response slot, a drained TMEM accumulator): the reads are complete before the
 // arrive executes (their values are in registers: the response was decoded, and
