@@ -221,6 +221,34 @@ def test_k_zero_gives_zero(b200):
     assert torch.all(c == 0)
 
 
+@pytest.mark.parametrize("variant", ["2cta", "2cta_clc", "persistent", "2cta_streamk"])
+def test_back_to_back_launches_see_each_others_results(b200, variant):
+    """Launches overlap their set-up with the previous kernel (programmatic dependent
+    launch) and wait before any global access. A chain on one stream, each GEMM
+    reading the previous one's output (read after write) and overwriting a buffer the
+    previous one read (write after read), equals the same chain run one GEMM at a time."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(71)
+    n = 1024
+    x0 = (torch.rand((n, n), generator=g, device="cuda") - 0.5).half()
+    ws = [((torch.rand((n, n), generator=g, device="cuda") - 0.5) * 0.06).half() for _ in range(6)]
+
+    def chain(sync_each):
+        x, y = x0.clone(), torch.empty_like(x0)
+        for w in ws:
+            b200.gemm(x, w, y, variant=variant)   # reads x (written by the previous GEMM)
+            if sync_each:
+                torch.cuda.synchronize()
+            x, y = y, x                            # the next GEMM overwrites what this one read
+        torch.cuda.synchronize()
+        return x.float().cpu().numpy()
+
+    ref = chain(True)
+    for _ in range(3):
+        assert np.array_equal(chain(False), ref)
+    assert np.isfinite(ref).all() and np.abs(ref).max() > 0
+
+
 def test_output_dtypes_agree(b200, oracle):
     inp = make_inputs(oracle, 256, 512, 512, "f16", 31, 32)
     outs = {o: _run(b200, inp, "persistent", o)[0] for o in ("f16", "bf16", "f32")}
