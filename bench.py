@@ -346,7 +346,14 @@ def run_ours(args):
         cpu = cpu_baseline(a, b, budget_s=args.cpu_budget)
 
     peaks = measured_peaks()
-    peak = peaks["bf16"]
+    # Denominator: the sustained cuBLAS figure when the power cap throttled the clock
+    # during our timed region (a long run of back-to-back launches, like the sustained
+    # measurement), else the burst figure; both fractions are reported.
+    capped = "sw_power_cap" in (clk.summary().get("reasons") or [])
+    burst = peaks["bf16"]
+    peak = peaks["bf16_sustained"] if capped and peaks.get("bf16_sustained") else burst
+    peak_kind = (f"bf16 dense cuBLAS {'sustained' if peak != burst else 'burst'} ({peaks['source']})"
+                 + ("; sw_power_cap active in the timed region" if capped else ""))
     result = {
         "metric": "GEMM TFLOPS fp16 & fp8 at 8192^3 per B200 and 8-GPU box; % of dense tensor peak",
         "value": round(value, 2),
@@ -367,13 +374,15 @@ def run_ours(args):
         "pct_of_peak": round(value / world / peak, 4) if peak else None,
         "roofline": {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4) if peak else None,
-                     "peak_kind": f"bf16 dense cuBLAS burst ({peaks['source']})",
+                     "peak_kind": peak_kind, "peak_burst": burst,
+                     "frac_burst": round(kernel_tflops / burst, 4) if burst else None,
                      "traffic": profile_traffic("f16_8192"),
                      "algorithmic_bytes": 3 * M * N * 2},
         "fp8": {"value": round(fp8_value, 2), "unit": "TFLOPS", "kernel_tflops": round(fp8_kernel, 2),
                 "peak_tflops": 2 * peak if peak else None,
                 "frac": round(fp8_kernel / (2 * peak), 4) if peak else None,
-                "peak_kind": "2 x measured bf16 (e4m3 dense rate is twice bf16)",
+                "frac_burst": round(fp8_kernel / (2 * burst), 4) if burst else None,
+                "peak_kind": "2 x the bf16 figure above (the e4m3 dense rate is twice bf16)",
                 "config": "e4m3 8192^3, per-tensor scales amax/448, bf16 C",
                 "traffic": profile_traffic("e4m3_8192"), "clocks": clk8.summary(),
                 "launch_ms": launch_stats(per8)},
