@@ -161,6 +161,13 @@ def timed_loop(torch, fn, steps: int, warmup: int, stream):
     return t0.elapsed_time(t1), per
 
 
+def load_multigpu():
+    spec = importlib.util.spec_from_file_location("b200_multigpu", ROOT / "hopper-lab_b200" / "multigpu.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def launch_stats(per):
     """Min / median / mean of the per-launch event times of one rank (ms)."""
     return {"min": round(min(per), 5), "median": round(statistics.median(per), 5),
@@ -328,17 +335,55 @@ def run_ours(args):
     e2e_value = FLOPS_8192 * world * e2e_steps / (float(te.item()) * 1e-3) / 1e12
 
     # ---------------- optional all-gather of C over NVLink (timed separately) ----
+    # (1) sequential: the GEMM, then NCCL all-gather of the slabs and the re-layout to
+    #     M x (N * world); (2) fused: b200_gemm_allgather stores every C tile into the
+    #     symmetric M x (N * world) buffer of every rank from the GEMM epilogue (NVLink
+    #     multicast where available), then a signal-pad barrier. Max over ranks.
     allgather = None
     if world > 1 and args.allgather:
+        mg = load_multigpu()
         gathered = torch.empty((world, M, N), dtype=torch.float16, device=dev)
-        ag = lambda: dist.all_gather_into_tensor(gathered, c)  # noqa: E731
+        out_full = torch.empty((M, N * world), dtype=torch.float16, device=dev)
+
+        def seq_step():
+            step()
+            dist.all_gather_into_tensor(gathered, c)
+            out_full.view(M, world, N).copy_(gathered.permute(1, 0, 2))
+
+        gc = mg.GatheredC(M, N * world, torch.float16, dev)
+        n0, n1 = gc.slab()
+
+        def fused_step():
+            gc.gemm(b200, a, b, c, stream=handle)
+            gc.sync()
+
+        def timed_max(fn, reps=10):
+            barrier()
+            total, per_rep = timed_loop(torch, fn, reps, 2, stream)
+            barrier()
+            t = torch.tensor([total / reps], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            if os.environ.get("B200_BENCH_DEBUG"):
+                print(f"rank {rank} {fn.__name__} per-rep ms {[round(x, 3) for x in per_rep]}", file=sys.stderr)
+            return float(t.item()), launch_stats(per_rep)
+
+        seq_ms, seq_stats = timed_max(seq_step)
+        fused_ms, fused_stats = timed_max(fused_step)
+        fused_rc, fused_bits = b200.status(handle)
+        # the fused result equals the sequential one, bit for bit
         barrier()
-        ag_total, _ = timed_loop(torch, ag, 10, 2, stream)
-        barrier()
-        ta = torch.tensor([ag_total / 10], device=dev, dtype=torch.float64)
-        dist.all_reduce(ta, op=dist.ReduceOp.MAX)
-        allgather = {"ms": float(ta.item()), "bytes_per_rank": M * N * 2 * world}
-        del gathered
+        same = torch.equal(gc.buf, out_full)
+        flag = torch.tensor([0 if same else 1], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        allgather = {"gemm_ms": round(max_ms / args.steps, 4),
+                     "sequential_ms": round(seq_ms, 4), "fused_ms": round(fused_ms, 4),
+                     "fused_mode": "multicast" if gc.multicast else "peers",
+                     "sequential_step_ms": seq_stats, "fused_step_ms": fused_stats,
+                     "fused_equals_sequential": int(flag.item()) == 0,
+                     "fused_device_status": int(fused_bits),
+                     "bytes_received_per_rank": M * N * 2 * (world - 1),
+                     "note": "sequential = GEMM + ncclAllGather + re-layout; fused = b200_gemm_allgather + barrier"}
+        del gathered, out_full, gc
 
     # ---------------- CPU baseline (rank 0, N = 1 only) ----------------
     cpu = None

@@ -47,7 +47,9 @@ EXPORTS = [
     "b200_quantize_e4m3",
     "b200_gemm_abi_version",
     "b200_gemm_noalloc",
+    "b200_gemm_allgather",
 ]
+GATHER_MULTICAST, GATHER_PEERS = 1, 2
 
 
 class GemmArgs(C.Structure):
@@ -110,6 +112,9 @@ def lib():
         L.b200_quantize_e4m3.restype = C.c_int
         L.b200_gemm_abi_version.argtypes = []
         L.b200_gemm_abi_version.restype = C.c_int
+        L.b200_gemm_allgather.argtypes = [C.POINTER(GemmArgs), C.c_void_p, C.c_int32, C.c_int32,
+                                          C.c_int64, C.c_int64, C.c_void_p]
+        L.b200_gemm_allgather.restype = C.c_int
         _LIB = L
     return _LIB
 
@@ -225,6 +230,20 @@ def gemm(a, b, c=None, *, out_dtype="bf16", scale_a=None, scale_b=None, variant=
     rc = lib().b200_gemm(C.byref(args), C.c_void_p(_stream_handle(stream)))
     if rc != OK:
         raise B200Error(rc, "b200_gemm")
+    return c
+
+
+def gemm_allgather(a, b, c, dst: int, mode: int, npeers: int, ldg: int, col_off: int, *,
+                   scale_a=None, scale_b=None, variant="auto", tile_n: int = 0, stream=None):
+    """b200_gemm_allgather: C = scale_a*scale_b*A.B^T on this GPU, and every C tile also
+    stored at G[row*ldg + col_off + col] on every GPU of the node. `dst` is the multicast
+    address of G (mode GATHER_MULTICAST) or the device address of an array of `npeers`
+    peer base addresses (GATHER_PEERS). The caller synchronises the GPUs before reading G."""
+    args = make_args(a, b, c, scale_a=scale_a, scale_b=scale_b, variant=variant, tile_n=tile_n)
+    rc = lib().b200_gemm_allgather(C.byref(args), C.c_void_p(dst), mode, npeers, ldg, col_off,
+                                   C.c_void_p(_stream_handle(stream)))
+    if rc != OK:
+        raise B200Error(rc, "b200_gemm_allgather")
     return c
 
 

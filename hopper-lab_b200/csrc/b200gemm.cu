@@ -254,7 +254,7 @@ namespace b200 {
 // `sms` / `cc_major` describe the current device, and `status` is the device word
 // the kernel's bounded waits report into.
 int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc_major,
-                     uint32_t* status, bool allow_workspace) {
+                     uint32_t* status, bool allow_workspace, const GatherSpec* gather) {
   int rc = B200_OK;
   if (cc_major != 10) return B200_ERR_UNSUPPORTED;
   const int ec = elem_bytes(a.c_dtype);
@@ -307,6 +307,13 @@ int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc
   kp.scale_b = a.scale_b;
   kp.status = status;
   kp.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kDefaultWaitNs;
+  if (gather) {
+    kp.gather = static_cast<const uint8_t*>(gather->dst);
+    kp.gather_mode = gather->mode;
+    kp.gather_peers = gather->peers;
+    kp.gather_ld = gather->ld;
+    kp.gather_col = gather->col;
+  }
 
   const uint32_t n_sms = uint32_t(sms);
   uint32_t grid = 0;
@@ -461,6 +468,42 @@ int b200_gemm(const B200GemmArgs* args, void* stream_v) {
   rc = device_setup(&dev);
   if (rc != B200_OK) return rc;
   return b200::gemm_launch_impl(a, stream, g_sm_count[dev], g_cc_major[dev], g_status[dev]);
+}
+
+int b200_gemm_allgather(const B200GemmArgs* args, const void* dst, int32_t mode, int32_t npeers,
+                        int64_t ldg, int64_t col_off, void* stream_v) {
+  int rc = validate(args);
+  if (rc != B200_OK) return rc;
+  const B200GemmArgs& a = *args;
+  if (!dst || (mode != B200_GATHER_MULTICAST && mode != B200_GATHER_PEERS)) return B200_ERR_INVALID_ARG;
+  if (mode == B200_GATHER_PEERS && (npeers < 1 || npeers > 64)) return B200_ERR_INVALID_ARG;
+  if (a.M == 0 || a.N == 0) return B200_OK;
+  if (a.K == 0) return B200_ERR_SHAPE;  // the gathered copy is written by the GEMM epilogue
+  const int64_t ec = elem_bytes(a.c_dtype);
+  if (ldg < 0 || col_off < 0 || ldg < col_off + a.N) return B200_ERR_SHAPE;
+  if ((a.N * ec) % 16 || (ldg * ec) % 16 || (col_off * ec) % 16 || !aligned16(dst)) return B200_ERR_ALIGN;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  int dev = 0;
+  rc = device_setup(&dev);
+  if (rc != B200_OK) return rc;
+  // Static schedules only. With the cluster-launch-control schedule, multicast
+  // (multimem) stores from the epilogue made launches stall intermittently until the
+  // kernel's 1 s bounded waits fired (measured on 2 GPUs; the same launches with peer
+  // stores, or with the static schedule, never did), so AUTO maps to the static
+  // counterpart and an explicit CLC or stream-K request is refused.
+  B200GemmArgs a2 = a;
+  if (a2.variant == B200_VARIANT_AUTO) {
+    int v = pick_variant(&a2, g_sm_count[dev], /*allow_workspace=*/false);
+    if (v == B200_VARIANT_2CTA_CLC) v = B200_VARIANT_2CTA;
+    if (v == B200_VARIANT_CLC) v = B200_VARIANT_PERSISTENT;
+    a2.variant = v;
+  } else if (a2.variant != B200_VARIANT_1CTA && a2.variant != B200_VARIANT_PERSISTENT &&
+             a2.variant != B200_VARIANT_2CTA) {
+    return B200_ERR_UNSUPPORTED;
+  }
+  b200::GatherSpec g{dst, uint32_t(mode), uint32_t(mode == B200_GATHER_PEERS ? npeers : 0), uint64_t(ldg),
+                     uint64_t(col_off)};
+  return b200::gemm_launch_impl(a2, stream, g_sm_count[dev], g_cc_major[dev], g_status[dev], false, &g);
 }
 
 int b200_gemm_status(void* stream_v, int clear, uint32_t* bits) {

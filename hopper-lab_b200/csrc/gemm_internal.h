@@ -21,7 +21,16 @@ int gemm_resolve_driver();
 // `allow_workspace` = false keeps the launch away from every schedule that needs
 // library-owned device memory (stream-K): AUTO never picks it, an explicit request
 // returns B200_ERR_SCRATCH_LIMIT.
+// Fused all-gather of C (b200_gemm_allgather); validated by the caller.
+struct GatherSpec {
+  const void* dst;
+  uint32_t mode;   // B200_GATHER_MULTICAST or B200_GATHER_PEERS
+  uint32_t peers;  // pointers in the array (GATHER_PEERS)
+  uint64_t ld;     // row pitch of the gathered matrix, elements
+  uint64_t col;    // this GPU's first column, elements
+};
+
 int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc_major,
-                     uint32_t* status, bool allow_workspace = true);
+                     uint32_t* status, bool allow_workspace = true, const GatherSpec* gather = nullptr);
 
 }  // namespace b200

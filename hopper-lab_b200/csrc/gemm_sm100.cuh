@@ -82,7 +82,17 @@ struct KParams {
   float* sk_work;
   uint32_t* sk_flags;
   uint32_t sk_epoch;
+  // Fused all-gather of C (b200_gemm_allgather): every C tile is also stored at
+  // gather[row * gather_ld + gather_col + col] on every GPU of the node.
+  //   GATHER_MULTICAST: `gather` is a multicast (NVLS) address, one multimem.st per 16 B
+  //   GATHER_PEERS    : `gather` is a device array of `gather_peers` peer-mapped bases
+  const uint8_t* gather;
+  uint32_t gather_mode;
+  uint32_t gather_peers;
+  uint64_t gather_ld;   // elements
+  uint64_t gather_col;  // elements
 };
+enum : uint32_t { GATHER_OFF = 0, GATHER_MULTICAST = 1, GATHER_PEERS = 2 };
 
 // A unit of work of one CTA (pair): k-blocks [kb0, kb1) of a tile.
 //   FULL    the whole K range: store C
@@ -804,10 +814,35 @@ __global__ void __launch_bounds__(384, 1)
           }
           fence_proxy_async_shared();
           __syncwarp();
+          const uint32_t col0 = bn * Cfg::BN + h * Cfg::MMA_N + (c0 + cc) * Cfg::EPI_COLS;
           if (lane == 0) {
-            const uint32_t col0 = bn * Cfg::BN + h * Cfg::MMA_N + (c0 + cc) * Cfg::EPI_COLS;
             if (uint32_t(row0) < p.M && col0 < p.N) tma_store_2d(&tmC, sb, int32_t(col0), row0);
             bulk_commit();
+          }
+          if (p.gather_mode != GATHER_OFF) {
+            // The staged 32 x 128-byte chunk again, read row-contiguously (8 lanes per
+            // row, 16 bytes each) and stored into every GPU's gathered C; the host
+            // checked that N, the pitch and the column offset keep 16-byte chunks
+            // whole and aligned.
+            const uint32_t j = lane & 7u;
+            const uint32_t col = col0 + j * (16u / Cfg::CD_BYTES);
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {
+              const uint32_t rr = 4u * i + (lane >> 3);
+              uint32_t x0, x1, x2, x3;
+              ld_shared_v4(sb + rr * 128u + ((j ^ (rr & 7u)) << 4), x0, x1, x2, x3);
+              const uint32_t grow = uint32_t(row0) + rr;
+              if (grow < p.M && col < p.N) {
+                const uint64_t off = (uint64_t(grow) * p.gather_ld + p.gather_col + col) * Cfg::CD_BYTES;
+                if (p.gather_mode == GATHER_MULTICAST) {
+                  multimem_st_v4(reinterpret_cast<uint64_t>(p.gather) + off, x0, x1, x2, x3);
+                } else {
+                  const uint64_t* bases = reinterpret_cast<const uint64_t*>(p.gather);
+                  for (uint32_t g = 0; g < p.gather_peers; ++g)
+                    *reinterpret_cast<uint4*>(bases[g] + off) = make_uint4(x0, x1, x2, x3);
+                }
+              }
+            }
           }
         }
       }
@@ -817,6 +852,8 @@ __global__ void __launch_bounds__(384, 1)
       more = next_more;
     }
     if (lane == 0) bulk_wait<0>();
+    // gathered stores to other GPUs are performed before the kernel is seen complete
+    if (p.gather_mode != GATHER_OFF) __threadfence_system();
     __syncwarp();
   }
 

@@ -258,6 +258,17 @@ __device__ __forceinline__ void bulk_copy_s2c(uint32_t dst_cluster, uint32_t src
       : "memory");
 }
 
+// One 16-byte store to a multicast (NVLS) address: the NVSwitch delivers it to the
+// same offset of every GPU bound to the multicast object. Bitwise: the four words are
+// moved as they are (typed f32 only because the instruction names a type).
+__device__ __forceinline__ void multimem_st_v4(uint64_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                               uint32_t d) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr),
+               "f"(__uint_as_float(a)), "f"(__uint_as_float(b)), "f"(__uint_as_float(c)),
+               "f"(__uint_as_float(d))
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

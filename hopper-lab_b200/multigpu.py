@@ -5,7 +5,11 @@ The reference has no multi-GPU code; BASELINE's config-5 shape
 replicated), the contiguous row slab B[n0:n1, :] of B (N x K, K contiguous) and
 writes its own slab C_g = A . B[n0:n1]^T (M x (n1-n0), contiguous). The compute
 needs no exchange. An optional all-gather of the C slabs over NVLink (NCCL) gives
-[G][M][N/G]; `relayout_gathered` turns that into row-major M x N.
+[G][M][N/G]; `relayout_gathered` turns that into row-major M x N. `GatheredC` is the
+fused alternative: the GEMM epilogue itself stores every C tile into a symmetric
+M x N buffer on every GPU (one multimem store through the NVSwitch per 16 bytes, or
+peer stores where the node has no NVLink multicast), so the gather overlaps the
+remaining tiles' math and needs no re-layout.
 
 Host logic only (plain integer arithmetic plus torch.distributed calls); the GEMM
 itself is b200_gemm on each rank's device.
@@ -60,6 +64,56 @@ def gemm_shard(b200, a, b_full_or_slab, c_slab, rank: int, world: int, slab_give
     if b_slab.shape[0] == 0:
         return c_slab
     return b200.gemm(a, b_slab, c_slab, **kw)
+
+
+class GatheredC:
+    """Row-major M x N output allocated in symmetric memory on every rank of `group`,
+    written by b200_gemm_allgather from every rank's C slab.
+
+    The buffer comes from torch.distributed._symmetric_memory (PyTorch is the plumbing
+    here: it allocates the peer-mapped memory, binds it to an NVLink multicast object
+    when the node supports one and exchanges the handles over the process group).
+    """
+
+    def __init__(self, m: int, n: int, dtype, device, group=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.m, self.n = m, n
+        self.buf = symm_mem.empty((m, n), dtype=dtype, device=device)
+        self.handle = symm_mem.rendezvous(self.buf, self.group)
+        # 0 when the node has no NVLink multicast (NVLS) for this buffer
+        self.multicast = int(self.handle.multicast_ptr) != 0
+        # device array of every rank's base address (GATHER_PEERS)
+        self.peer_bases = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64,
+                                       device=device)
+
+    def slab(self, n_total: int | None = None) -> tuple[int, int]:
+        return shard_columns(n_total or self.n, self.world, self.rank)
+
+    def gemm(self, b200, a, b_slab, c_slab, *, force_peers: bool = False, stream=None, **kw):
+        """This rank's C slab = A . B_slab^T, stored locally into `c_slab` and into the
+        gathered buffer of every rank at this rank's columns. Queued on `stream`."""
+        n0, n1 = self.slab()
+        if n1 - n0 != b_slab.shape[0]:
+            raise ValueError("B slab does not match this rank's columns")
+        if n1 == n0:
+            return c_slab
+        if self.multicast and not force_peers:
+            dst, mode, npeers = self.handle.multicast_ptr, b200.GATHER_MULTICAST, 0
+        else:
+            dst, mode, npeers = self.peer_bases.data_ptr(), b200.GATHER_PEERS, self.world
+        return b200.gemm_allgather(a, b_slab, c_slab, dst, mode, npeers, self.n, n0, stream=stream,
+                                   **kw)
+
+    def sync(self):
+        """Every rank's gathered stores are complete and visible (a barrier on the
+        symmetric memory's signal pads, queued on the current stream)."""
+        self.handle.barrier(channel=0)
 
 
 def all_gather_columns(c_slab, world: int, group=None):

@@ -141,6 +141,30 @@ int b200_gemm_pick_variant(const B200GemmArgs* args);
  * reference. */
 int b200_gemm_noalloc(const B200GemmArgs* args, void* stream, int check_status);
 
+/* Fused GEMM + all-gather of C across the GPUs of one node. Computes this GPU's
+ * C = scale_a*scale_b*A.B^T exactly as b200_gemm does (C is written locally too) and,
+ * from the same epilogue, stores every finished C tile into the gathered matrix G of
+ * every GPU: G[row * ldg + col_off + col] = C[row][col], element type of C. The
+ * transfer runs tile by tile under the main loop of the following tiles, over NVLink:
+ *   B200_GATHER_MULTICAST  `dst` is the multicast (NVLS) address of a buffer bound on
+ *                          every GPU; one multimem.st per 16 bytes reaches all of them
+ *                          through the NVSwitch.
+ *   B200_GATHER_PEERS      `dst` is a device array of `npeers` uint64 base addresses of
+ *                          peer-mapped buffers (this GPU's own included); each tile is
+ *                          stored to every one of them.
+ * Requirements (else B200_ERR_ALIGN / B200_ERR_SHAPE / B200_ERR_INVALID_ARG): K > 0;
+ * N, ldg and col_off keep 16-byte chunks of C whole and aligned (N * elem, ldg * elem
+ * and col_off * elem multiples of 16); ldg >= col_off + N; dst 16-byte aligned (and
+ * every base in the array). On return the launch is queued; G is complete on a GPU
+ * once every GPU's launch has completed, so the caller synchronises the GPUs (e.g. a
+ * barrier on the symmetric-memory signal pads) before reading G. Static schedules
+ * only: AUTO resolves to 1CTA / PERSISTENT / 2CTA; other variants return
+ * B200_ERR_UNSUPPORTED. The reference has no
+ * multi-GPU code; its planned counterpart is a separate ncclAllGather after the GEMM. */
+enum { B200_GATHER_MULTICAST = 1, B200_GATHER_PEERS = 2 };
+int b200_gemm_allgather(const B200GemmArgs* args, const void* dst, int32_t mode, int32_t npeers,
+                        int64_t ldg, int64_t col_off, void* stream);
+
 /* Per-tensor e4m3 quantiser on the device: *scale = amax(|x|)/448 (1 when all
  * x == 0) and q[i] = e4m3_rn_satfinite(x[i] / *scale). Device pointers: x (fp32,
  * 16-byte aligned), q (n bytes, 8-byte aligned), scale (one fp32). Replaces the

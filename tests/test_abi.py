@@ -188,3 +188,19 @@ def test_noalloc_refuses_streamk_without_touching_the_device(b200):
     fn.restype = C.c_int
     a = _args(b200, variant=b200.VARIANTS["2cta_streamk"])
     assert fn(C.byref(a), None, 0) == b200.ERR_SCRATCH_LIMIT
+
+
+def test_allgather_entry_point_validates_without_a_gpu(b200):
+    """b200_gemm_allgather checks its gather arguments before any CUDA call."""
+    L = b200.lib()
+    a = _args(b200)
+    dst = C.c_void_p(0x40000)
+    assert L.b200_gemm_allgather(C.byref(a), None, 1, 0, 512, 0, None) == b200.ERR_INVALID_ARG
+    assert L.b200_gemm_allgather(C.byref(a), dst, 3, 0, 512, 0, None) == b200.ERR_INVALID_ARG
+    assert L.b200_gemm_allgather(C.byref(a), dst, 2, 0, 512, 0, None) == b200.ERR_INVALID_ARG
+    assert L.b200_gemm_allgather(C.byref(a), dst, 1, 0, 248, 0, None) == b200.ERR_SHAPE      # ldg < N
+    assert L.b200_gemm_allgather(C.byref(a), dst, 1, 0, 512, 264, None) == b200.ERR_SHAPE    # past ldg
+    assert L.b200_gemm_allgather(C.byref(a), dst, 1, 0, 520, 4, None) == b200.ERR_ALIGN      # 8-byte col
+    assert L.b200_gemm_allgather(C.byref(a), C.c_void_p(0x40008), 1, 0, 512, 0, None) == b200.ERR_ALIGN
+    k0 = _args(b200, K=0)
+    assert L.b200_gemm_allgather(C.byref(k0), dst, 1, 0, 512, 0, None) == b200.ERR_SHAPE
