@@ -48,6 +48,9 @@ EXPORTS = [
     "b200_gemm_abi_version",
     "b200_gemm_noalloc",
     "b200_gemm_allgather",
+    "b200_gemm_plan_create",
+    "b200_gemm_plan_launch",
+    "b200_gemm_plan_destroy",
 ]
 GATHER_MULTICAST, GATHER_PEERS = 1, 2
 
@@ -115,6 +118,12 @@ def lib():
         L.b200_gemm_allgather.argtypes = [C.POINTER(GemmArgs), C.c_void_p, C.c_int32, C.c_int32,
                                           C.c_int64, C.c_int64, C.c_void_p]
         L.b200_gemm_allgather.restype = C.c_int
+        L.b200_gemm_plan_create.argtypes = [C.POINTER(GemmArgs), C.POINTER(C.c_void_p)]
+        L.b200_gemm_plan_create.restype = C.c_int
+        L.b200_gemm_plan_launch.argtypes = [C.c_void_p, C.c_void_p]
+        L.b200_gemm_plan_launch.restype = C.c_int
+        L.b200_gemm_plan_destroy.argtypes = [C.c_void_p]
+        L.b200_gemm_plan_destroy.restype = None
         _LIB = L
     return _LIB
 
@@ -245,6 +254,38 @@ def gemm_allgather(a, b, c, dst: int, mode: int, npeers: int, ldg: int, col_off:
     if rc != OK:
         raise B200Error(rc, "b200_gemm_allgather")
     return c
+
+
+class Plan:
+    """b200_gemm_plan_*: a GEMM resolved once (variant, tensor maps, kernel parameters)
+    on fixed buffers; `launch()` only launches. Keeps references to the tensors so the
+    buffers outlive the plan."""
+
+    def __init__(self, a, b, c, **kw):
+        self._h = None
+        self._keep = (a, b, c, kw.get("scale_a"), kw.get("scale_b"))
+        args = make_args(a, b, c, **kw)
+        h = C.c_void_p()
+        rc = lib().b200_gemm_plan_create(C.byref(args), C.byref(h))
+        if rc != OK:
+            raise B200Error(rc, "b200_gemm_plan_create")
+        self._h = h
+
+    def launch(self, stream=None):
+        rc = lib().b200_gemm_plan_launch(self._h, C.c_void_p(_stream_handle(stream)))
+        if rc != OK:
+            raise B200Error(rc, "b200_gemm_plan_launch")
+
+    def close(self):
+        if self._h:
+            lib().b200_gemm_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def gemm_raw(args: GemmArgs, stream=None) -> int:

@@ -14,6 +14,7 @@
 #include <cstring>
 #include <atomic>
 #include <mutex>
+#include <new>
 
 #include "b200gemm.h"
 #include "gemm_internal.h"
@@ -250,18 +251,25 @@ int pick_variant(const B200GemmArgs* a, int sms, bool allow_workspace) {
 
 namespace b200 {
 
-// Launch body shared by the C-ABI entry points: `a` is validated and non-empty,
+// Everything of a launch but the launch itself: `a` is validated and non-empty,
 // `sms` / `cc_major` describe the current device, and `status` is the device word
-// the kernel's bounded waits report into.
-int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc_major,
-                     uint32_t* status, bool allow_workspace, const GatherSpec* gather) {
+// the kernel's bounded waits report into. Shared by the C-ABI entry points and the
+// plan objects (which keep the result and only launch).
+int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status, bool allow_workspace,
+                 const GatherSpec* gather, Prepared* out) {
   int rc = B200_OK;
   if (cc_major != 10) return B200_ERR_UNSUPPORTED;
   const int ec = elem_bytes(a.c_dtype);
+  std::memset(out, 0, sizeof(*out));
+  if (cudaGetDevice(&out->dev) != cudaSuccess || out->dev < 0 || out->dev >= 64) return B200_ERR_CUDA;
 
   if (a.K == 0) {  // empty reduction: C = 0
-    cudaError_t e = cudaMemset2DAsync(a.C, size_t(a.ldc) * ec, 0, size_t(a.N) * ec, size_t(a.M), stream);
-    return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+    out->memset_only = true;
+    out->c = a.C;
+    out->c_pitch = size_t(a.ldc) * ec;
+    out->c_width = size_t(a.N) * ec;
+    out->c_height = size_t(a.M);
+    return B200_OK;
   }
 
   const int variant = (a.variant == B200_VARIANT_AUTO) ? pick_variant(&a, sms, allow_workspace) : a.variant;
@@ -278,7 +286,9 @@ int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc
   const uint32_t stage_k = bk * vs.atoms;
   const uint32_t cd_cols = 128u / uint32_t(ec);
 
-  alignas(64) CUtensorMap tA, tB, tC;
+  CUtensorMap& tA = out->tA;
+  CUtensorMap& tB = out->tB;
+  CUtensorMap& tC = out->tC;
   rc = encode_2d(&tA, a.A, a.ab_dtype, uint64_t(a.M), uint64_t(a.K), uint64_t(a.lda), 128u, bk);
   if (rc != B200_OK) return rc;
   rc = encode_2d(&tB, a.B, a.ab_dtype, uint64_t(a.N), uint64_t(a.K), uint64_t(a.ldb),
@@ -287,8 +297,7 @@ int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc
   rc = encode_2d(&tC, a.C, a.c_dtype, uint64_t(a.M), uint64_t(a.N), uint64_t(a.ldc), 32u, cd_cols);
   if (rc != B200_OK) return rc;
 
-  KParams kp;
-  std::memset(&kp, 0, sizeof(kp));
+  KParams& kp = out->kp;
   kp.M = uint32_t(a.M);
   kp.N = uint32_t(a.N);
   kp.K = uint32_t(a.K);
@@ -341,33 +350,51 @@ int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc
       const uint32_t pairs = n_sms / 2;
       const uint32_t workers = uint32_t(iters < pairs ? iters : pairs);
       grid = 2u * workers;
-      int dev = 0;
-      if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B200_ERR_CUDA;
-      rc = streamk_workspace(dev, &kp.sk_work, &kp.sk_flags);
+      rc = streamk_workspace(out->dev, &kp.sk_work, &kp.sk_flags);
       if (rc != B200_OK) return rc;
-      uint32_t ep = g_sk_epoch[dev].fetch_add(1) + 1;
-      if (ep == 0) ep = g_sk_epoch[dev].fetch_add(1) + 1;  // 0 is the flags' initial value
-      kp.sk_epoch = ep;
+      out->streamk = true;  // a fresh epoch is taken at every launch
       break;
     }
     default: return B200_ERR_INVALID_ARG;
   }
 
-  LaunchPlan lp;
-  lp.a = &tA;
-  lp.b = &tB;
-  lp.c = &tC;
-  lp.kp = kp;
-  lp.grid = grid;
-  lp.stream = stream;
+  out->grid = grid;
   // smem_bytes() depends only on the stage size, identical for every dtype.
-  lp.smem = variant_smem(vs, stages);
+  out->smem = variant_smem(vs, stages);
+  out->ab = a.ab_dtype;
+  out->cd = a.c_dtype;
+  out->cg = vs.cg;
+  out->sched = vs.sched;
+  out->nh = vs.nh;
+  return B200_OK;
+}
+
+// Launch a prepared GEMM on `stream` (the current device must be the one it was
+// prepared on).
+int gemm_launch_prepared(Prepared& pr, cudaStream_t stream) {
+  if (pr.memset_only) {
+    cudaError_t e = cudaMemset2DAsync(pr.c, pr.c_pitch, 0, pr.c_width, pr.c_height, stream);
+    return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
+  }
+  if (pr.streamk) {
+    uint32_t ep = g_sk_epoch[pr.dev].fetch_add(1) + 1;
+    if (ep == 0) ep = g_sk_epoch[pr.dev].fetch_add(1) + 1;  // 0 is the flags' initial value
+    pr.kp.sk_epoch = ep;
+  }
+  LaunchPlan lp;
+  lp.a = &pr.tA;
+  lp.b = &pr.tB;
+  lp.c = &pr.tC;
+  lp.kp = pr.kp;
+  lp.grid = pr.grid;
+  lp.stream = stream;
+  lp.smem = pr.smem;
 
   cudaError_t e;
-  switch (a.ab_dtype) {
-    case B200_DT_F16: e = b200::launch_f16(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
-    case B200_DT_BF16: e = b200::launch_bf16(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
-    default: e = b200::launch_e4m3(a.c_dtype, vs.cg, vs.sched, vs.nh, lp); break;
+  switch (pr.ab) {
+    case B200_DT_F16: e = b200::launch_f16(pr.cd, pr.cg, pr.sched, pr.nh, lp); break;
+    case B200_DT_BF16: e = b200::launch_bf16(pr.cd, pr.cg, pr.sched, pr.nh, lp); break;
+    default: e = b200::launch_e4m3(pr.cd, pr.cg, pr.sched, pr.nh, lp); break;
   }
   if (e == cudaErrorNotSupported) return B200_ERR_UNSUPPORTED;
   if (e != cudaSuccess) {
@@ -375,6 +402,14 @@ int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc
     return B200_ERR_LAUNCH;
   }
   return B200_OK;
+}
+
+int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc_major,
+                     uint32_t* status, bool allow_workspace, const GatherSpec* gather) {
+  Prepared pr;
+  int rc = gemm_prepare(a, sms, cc_major, status, allow_workspace, gather, &pr);
+  if (rc != B200_OK) return rc;
+  return gemm_launch_prepared(pr, stream);
 }
 
 }  // namespace b200
@@ -469,6 +504,44 @@ int b200_gemm(const B200GemmArgs* args, void* stream_v) {
   if (rc != B200_OK) return rc;
   return b200::gemm_launch_impl(a, stream, g_sm_count[dev], g_cc_major[dev], g_status[dev]);
 }
+
+struct B200GemmPlan {
+  bool empty;  // M == 0 or N == 0: launching does nothing
+  b200::Prepared pr;
+};
+
+int b200_gemm_plan_create(const B200GemmArgs* args, B200GemmPlan** plan) {
+  if (!plan) return B200_ERR_INVALID_ARG;
+  *plan = nullptr;
+  int rc = validate(args);
+  if (rc != B200_OK) return rc;
+  int dev = 0;
+  rc = device_setup(&dev);
+  if (rc != B200_OK) return rc;
+  B200GemmPlan* p = new (std::nothrow) B200GemmPlan();
+  if (!p) return B200_ERR_CUDA;
+  p->empty = args->M == 0 || args->N == 0;
+  if (!p->empty) {
+    rc = b200::gemm_prepare(*args, g_sm_count[dev], g_cc_major[dev], g_status[dev], true, nullptr, &p->pr);
+    if (rc != B200_OK) {
+      delete p;
+      return rc;
+    }
+  }
+  *plan = p;
+  return B200_OK;
+}
+
+int b200_gemm_plan_launch(B200GemmPlan* plan, void* stream_v) {
+  if (!plan) return B200_ERR_INVALID_ARG;
+  if (plan->empty) return B200_OK;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
+  if (dev != plan->pr.dev) return B200_ERR_INVALID_ARG;
+  return b200::gemm_launch_prepared(plan->pr, static_cast<cudaStream_t>(stream_v));
+}
+
+void b200_gemm_plan_destroy(B200GemmPlan* plan) { delete plan; }
 
 int b200_gemm_allgather(const B200GemmArgs* args, const void* dst, int32_t mode, int32_t npeers,
                         int64_t ldg, int64_t col_off, void* stream_v) {

@@ -1,11 +1,13 @@
 // gemm_internal.h — host-side helpers shared by the C-ABI translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
 
 #include "b200gemm.h"
+#include "gemm_sm100.cuh"
 
 namespace b200 {
 
@@ -32,5 +34,24 @@ struct GatherSpec {
 
 int gemm_launch_impl(const B200GemmArgs& a, cudaStream_t stream, int sms, int cc_major,
                      uint32_t* status, bool allow_workspace = true, const GatherSpec* gather = nullptr);
+
+// A launch with everything resolved: variant, tensor maps, kernel parameters, grid.
+struct Prepared {
+  alignas(64) CUtensorMap tA;
+  alignas(64) CUtensorMap tB;
+  alignas(64) CUtensorMap tC;
+  KParams kp;
+  uint32_t grid, smem;
+  int ab, cd, cg, sched, nh;
+  int dev;
+  bool streamk;      // takes a fresh workspace epoch per launch
+  bool memset_only;  // K == 0: C = 0
+  void* c;
+  size_t c_pitch, c_width, c_height;
+};
+
+int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status, bool allow_workspace,
+                 const GatherSpec* gather, Prepared* out);
+int gemm_launch_prepared(Prepared& pr, cudaStream_t stream);
 
 }  // namespace b200

@@ -141,6 +141,19 @@ int b200_gemm_pick_variant(const B200GemmArgs* args);
  * reference. */
 int b200_gemm_noalloc(const B200GemmArgs* args, void* stream, int check_status);
 
+/* Plans: everything b200_gemm resolves per call (argument checks, variant and tile
+ * choice, the three tensor maps, kernel parameters, grid) done once, for callers that
+ * launch the same GEMM on the same buffers repeatedly (serving loops, benchmark
+ * steps). A plan is bound to the pointers in `args` and to the current device at
+ * creation; b200_gemm_plan_launch only launches (B200_ERR_INVALID_ARG on another
+ * device). The reference encodes its tensor maps once per experiment and passes them
+ * to dispatch() (src/05_gemm/gemm_ws.cu:214-235); a plan is that split as an API.
+ * Plans own host memory only; destroy them with b200_gemm_plan_destroy. */
+typedef struct B200GemmPlan B200GemmPlan;
+int b200_gemm_plan_create(const B200GemmArgs* args, B200GemmPlan** plan);
+int b200_gemm_plan_launch(B200GemmPlan* plan, void* stream);
+void b200_gemm_plan_destroy(B200GemmPlan* plan);
+
 /* Fused GEMM + all-gather of C across the GPUs of one node. Computes this GPU's
  * C = scale_a*scale_b*A.B^T exactly as b200_gemm does (C is written locally too) and,
  * from the same epilogue, stores every finished C tile into the gathered matrix G of

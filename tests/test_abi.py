@@ -15,7 +15,7 @@ HEADER = ROOT / "include" / "b200gemm.h"
 def declared_functions():
     text = HEADER.read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(b200_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|void|const char\*)\s+(b200_\w+)\s*\(", text, flags=re.M)))
 
 
 def test_header_declares_the_python_export_list(b200):
@@ -204,3 +204,15 @@ def test_allgather_entry_point_validates_without_a_gpu(b200):
     assert L.b200_gemm_allgather(C.byref(a), C.c_void_p(0x40008), 1, 0, 512, 0, None) == b200.ERR_ALIGN
     k0 = _args(b200, K=0)
     assert L.b200_gemm_allgather(C.byref(k0), dst, 1, 0, 512, 0, None) == b200.ERR_SHAPE
+
+
+def test_plan_validates_without_a_gpu(b200):
+    """b200_gemm_plan_create checks its arguments before touching the device."""
+    L = b200.lib()
+    h = C.c_void_p()
+    assert L.b200_gemm_plan_create(C.byref(_args(b200)), None) == b200.ERR_INVALID_ARG
+    assert L.b200_gemm_plan_create(C.byref(_args(b200, ab_dtype=7)), C.byref(h)) == b200.ERR_INVALID_ARG
+    assert not h.value
+    assert L.b200_gemm_plan_create(C.byref(_args(b200, A=0x10001)), C.byref(h)) == b200.ERR_ALIGN
+    assert L.b200_gemm_plan_launch(None, None) == b200.ERR_INVALID_ARG
+    L.b200_gemm_plan_destroy(None)  # a null plan is accepted, like free(NULL)

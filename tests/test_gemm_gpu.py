@@ -249,6 +249,41 @@ def test_back_to_back_launches_see_each_others_results(b200, variant):
     assert np.isfinite(ref).all() and np.abs(ref).max() > 0
 
 
+@pytest.mark.parametrize("variant", ["auto", "2cta_clc", "2cta_streamk", "persistent", "1cta"])
+def test_plan_matches_per_call_launch(b200, variant):
+    """A plan (b200_gemm_plan_*) resolves the launch once; each plan launch gives
+    exactly what b200_gemm gives, stream-K plans included (each launch takes a fresh
+    workspace epoch)."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(91)
+    m, n, k = 1024, 1280, 4096
+    a = (torch.rand((m, k), generator=g, device="cuda") * 2 - 1).half()
+    b = (torch.rand((n, k), generator=g, device="cuda") * 2 - 1).half()
+    ref = b200.gemm(a, b, out_dtype="f16", variant=variant)
+    c = torch.full((m, n), float("nan"), dtype=torch.float16, device="cuda")
+    plan = b200.Plan(a, b, c, variant=variant)
+    for _ in range(3):
+        c.fill_(float("nan"))
+        plan.launch()
+        torch.cuda.synchronize()
+        assert torch.equal(c, ref)
+    plan.close()
+    rc, bits = b200.status()
+    assert rc == 0, hex(bits)
+
+
+def test_plan_edge_cases(b200):
+    a = torch.empty((64, 0), dtype=torch.float16, device="cuda")
+    b = torch.empty((32, 0), dtype=torch.float16, device="cuda")
+    c = torch.full((64, 32), 3.0, dtype=torch.float16, device="cuda")
+    b200.Plan(a, b, c).launch()  # K = 0: C = 0
+    torch.cuda.synchronize()
+    assert torch.all(c == 0)
+    e = torch.empty((0, 16), dtype=torch.float16, device="cuda")
+    b200.Plan(e, torch.zeros((16, 16), dtype=torch.float16, device="cuda"),
+              torch.empty((0, 16), dtype=torch.float16, device="cuda")).launch()  # M = 0: nothing
+
+
 def test_output_dtypes_agree(b200, oracle):
     inp = make_inputs(oracle, 256, 512, 512, "f16", 31, 32)
     outs = {o: _run(b200, inp, "persistent", o)[0] for o in ("f16", "bf16", "f32")}
