@@ -63,6 +63,10 @@ int g_cc_major[64] = {0};
 
 constexpr uint64_t kDefaultWaitNs = 1000000000ull;  // 1 s per wait
 constexpr int kDefaultGroupM = 8;
+// 256x512 tiles are twice as wide, so twice as many block-rows per group keep a wave's
+// A and B panels balanced: at 8192^3 under the power cap, 2-4 % less energy per GEMM
+// than G = 8 (f16 828 vs 843 mJ, e4m3 423 vs 439) and 0.4-1 % more throughput.
+constexpr int kDefaultGroupMWide = 16;
 
 int resolve_encode() {
   if (g_encode) return B200_OK;
@@ -310,7 +314,7 @@ int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status,
   if (variant == B200_VARIANT_2CTA_SHARE) kp.num_tiles = 2u * ((kp.m_tiles + 1u) / 2u) * kp.n_tiles;
   kp.k_blocks = uint32_t((a.K + stage_k - 1) / stage_k);
   kp.stages = stages;
-  kp.group_m = a.group_m ? uint32_t(a.group_m) : uint32_t(kDefaultGroupM);
+  kp.group_m = a.group_m ? uint32_t(a.group_m) : uint32_t(vs.nh == 2 ? kDefaultGroupMWide : kDefaultGroupM);
   kp.fault_inject = a.fault_inject ? 1u : 0u;
   kp.scale_a = a.scale_a;
   kp.scale_b = a.scale_b;
