@@ -16,14 +16,17 @@ loader of your own; it registers itself as ``hopper_lab_b200``.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "lib" / "libb200gemm.so"
+# The in-tree build; B200GEMM_LIB names another build of the same ABI (e.g. one made
+# with different compile-time options) to load instead.
+LIB_PATH = Path(os.environ.get("B200GEMM_LIB") or PKG / "lib" / "libb200gemm.so")
 
 DT_F16, DT_BF16, DT_E4M3, DT_F32 = 0, 1, 2, 3
 VARIANTS = {"auto": 0, "1cta": 1, "2cta": 2, "persistent": 3, "clc": 4, "2cta_clc": 5,
-            "2cta_streamk": 6, "2cta_share": 7}
+            "2cta_streamk": 6}
 VARIANT_NAMES = {v: k for k, v in VARIANTS.items()}
 
 OK = 0
@@ -44,6 +47,7 @@ EXPORTS = [
     "b200_gemm_status",
     "b200_gemm_variant_info",
     "b200_gemm_pick_variant",
+    "b200_gemm_pick_config",
     "b200_quantize_e4m3",
     "b200_gemm_abi_version",
     "b200_gemm_noalloc",
@@ -111,6 +115,9 @@ def lib():
         L.b200_gemm_variant_info.restype = C.c_int
         L.b200_gemm_pick_variant.argtypes = [C.POINTER(GemmArgs)]
         L.b200_gemm_pick_variant.restype = C.c_int
+        L.b200_gemm_pick_config.argtypes = [C.POINTER(GemmArgs), C.POINTER(C.c_int32),
+                                            C.POINTER(C.c_int32)]
+        L.b200_gemm_pick_config.restype = C.c_int
         L.b200_quantize_e4m3.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]
         L.b200_quantize_e4m3.restype = C.c_int
         L.b200_gemm_abi_version.argtypes = []
@@ -299,6 +306,15 @@ def pick_variant(a, b, c) -> str:
     if v < 0:
         raise B200Error(v, "pick_variant")
     return VARIANT_NAMES[v]
+
+
+def pick_config(args: GemmArgs) -> tuple[str, int]:
+    """(variant name, tile width) that b200_gemm launches for a prepared argument block."""
+    v, tn = C.c_int32(), C.c_int32()
+    rc = lib().b200_gemm_pick_config(C.byref(args), C.byref(v), C.byref(tn))
+    if rc != OK:
+        raise B200Error(rc, "pick_config")
+    return VARIANT_NAMES[v.value], tn.value
 
 
 def status(stream=None, clear: bool = True):

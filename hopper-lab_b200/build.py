@@ -90,7 +90,7 @@ EXPERIMENTS = {
     "peak_tcgen05": [],
     "cublaslt_ref": ["-lcublasLt"],
     "gemm_multi_gpu": ["-lnccl"],
-    "dsmem_copy": [],
+    "umma_desc_sweep": [],
 }
 
 

@@ -32,36 +32,62 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 std::mutex g_mu;
+// Per-device state, set up once. The pointers are published with release stores
+// after every field they guard is written, and read with acquire loads on the fast
+// path, so a thread that sees a pointer also sees the SM count and the rest.
+//
 // stream-K partial-tile workspace: one 128 x 256 fp32 region and one ready flag per
 // CTA slot (256 slots cover any grid on a 148-SM part), allocated on first use
 constexpr int kSkSlots = 256;
-float* g_sk_work[64] = {nullptr};
+std::atomic<float*> g_sk_work[64];
 uint32_t* g_sk_flags[64] = {nullptr};
 std::atomic<uint32_t> g_sk_epoch[64];
+// Stream-K launches on one device share that workspace, so they must not overlap on
+// the GPU. Launches on one stream are ordered by the stream; a launch on another
+// stream first waits (cudaStreamWaitEvent) for the event recorded after the previous
+// stream-K launch. g_sk_mu serialises the bookkeeping (host only).
+std::mutex g_sk_mu;
+cudaEvent_t g_sk_event[64] = {nullptr};
+cudaStream_t g_sk_last_stream[64] = {nullptr};
+bool g_sk_recorded[64] = {false};
 
 int streamk_workspace(int dev, float** work, uint32_t** flags) {
-  if (!g_sk_work[dev]) {
+  float* w = g_sk_work[dev].load(std::memory_order_acquire);
+  if (!w) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_sk_work[dev]) {
-      float* w = nullptr;
+    w = g_sk_work[dev].load(std::memory_order_relaxed);
+    if (!w) {
       uint32_t* f = nullptr;
+      cudaEvent_t ev = nullptr;
       if (cudaMalloc(&w, size_t(kSkSlots) * 128 * 256 * sizeof(float)) != cudaSuccess) return B200_ERR_CUDA;
       if (cudaMalloc(&f, size_t(kSkSlots) * sizeof(uint32_t)) != cudaSuccess) return B200_ERR_CUDA;
       if (cudaMemset(f, 0, size_t(kSkSlots) * sizeof(uint32_t)) != cudaSuccess) return B200_ERR_CUDA;
+      if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return B200_ERR_CUDA;
       g_sk_flags[dev] = f;
-      g_sk_work[dev] = w;
+      g_sk_event[dev] = ev;
+      g_sk_work[dev].store(w, std::memory_order_release);
     }
   }
-  *work = g_sk_work[dev];
+  *work = w;
   *flags = g_sk_flags[dev];
   return B200_OK;
 }
 EncodeTiledFn g_encode = nullptr;
-uint32_t* g_status[64] = {nullptr};
+std::atomic<uint32_t*> g_status[64];
 int g_sm_count[64] = {0};
 int g_cc_major[64] = {0};
 
 constexpr uint64_t kDefaultWaitNs = 1000000000ull;  // 1 s per wait
+// L2 cache policies of the operand loads and C stores (KParams::l2_policy bits): A
+// evict_last, B evict_first, C stores evict_first. Under the 1 kW power cap the clock
+// follows the energy of each GEMM, and these hints cut it: sustained 8192^3, 3 rounds
+// interleaved with cuBLASLt (bench.py --mode power), e4m3 2665-2701 TFLOPS and
+// 403-407 mJ per GEMM against 2578-2608 and 408-421 with evict_normal everywhere
+// (cuBLASLt 2616-2626), f16 1287-1294 against 1263-1276 (cuBLASLt 1306-1325).
+#ifndef B200_L2_POLICY
+#define B200_L2_POLICY 7u
+#endif
+constexpr uint32_t kL2Policy = B200_L2_POLICY;
 constexpr int kDefaultGroupM = 8;
 // 256x512 tiles are twice as wide, so twice as many block-rows per group keep a wave's
 // A and B panels balanced: at 8192^3 under the power cap, 2-4 % less energy per GEMM
@@ -85,9 +111,9 @@ int device_setup(int* dev_out) {
   if (cudaGetDevice(&dev) != cudaSuccess) return B200_ERR_CUDA;
   if (dev < 0 || dev >= 64) return B200_ERR_CUDA;
   *dev_out = dev;
-  if (g_status[dev]) return B200_OK;
+  if (g_status[dev].load(std::memory_order_acquire)) return B200_OK;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_status[dev]) return B200_OK;
+  if (g_status[dev].load(std::memory_order_relaxed)) return B200_OK;
   int rc = resolve_encode();
   if (rc != B200_OK) return rc;
   int sms = 0, major = 0;
@@ -100,9 +126,11 @@ int device_setup(int* dev_out) {
   if (cudaMemset(st, 0, 256) != cudaSuccess) return B200_ERR_CUDA;
   g_sm_count[dev] = sms;
   g_cc_major[dev] = major;
-  g_status[dev] = st;
+  g_status[dev].store(st, std::memory_order_release);
   return B200_OK;
 }
+
+uint32_t* status_word(int dev) { return g_status[dev].load(std::memory_order_acquire); }
 
 int elem_bytes(int dt) {
   switch (dt) {
@@ -141,19 +169,19 @@ int encode_2d(CUtensorMap* m, const void* ptr, int dt, uint64_t rows, uint64_t c
 }
 
 struct VariantShape {
-  int cg, sched, nh;
-  uint32_t tile_m, tile_n, max_stages, default_stages, atoms, smem_per_stage_cfg;
+  int cg, sched, tn;
+  uint32_t tile_m, tile_n, max_stages, default_stages, atoms;
 };
 
 // Tile and ring facts of one kernel configuration. Stage bytes do not depend on
 // the element type (one 128-byte K atom per row), so the f16 instantiation's
 // constants stand for every dtype.
-template <int CG, int SCHED, int NH>
+template <int CG, int SCHED, int TN>
 void fill_shape(VariantShape* vs) {
-  using Cfg = GemmCfg<b200::DT_F16, b200::DT_F16, CG, SCHED, NH>;
+  using Cfg = GemmCfg<b200::DT_F16, b200::DT_F16, CG, SCHED, TN>;
   vs->cg = CG;
   vs->sched = SCHED;
-  vs->nh = NH;
+  vs->tn = TN;
   vs->tile_m = uint32_t(Cfg::BM * CG);
   vs->tile_n = uint32_t(Cfg::BN);
   vs->max_stages = Cfg::MAX_STAGES;
@@ -161,40 +189,40 @@ void fill_shape(VariantShape* vs) {
   vs->atoms = uint32_t(Cfg::ATOMS);
 }
 
-template <int CG, int SCHED, int NH>
+template <int CG, int TN>
 uint32_t shape_smem(uint32_t stages) {
-  return GemmCfg<b200::DT_F16, b200::DT_F16, CG, SCHED, NH>::smem_bytes(stages);
+  return GemmCfg<b200::DT_F16, b200::DT_F16, CG, b200::SCHED_STATIC, TN>::smem_bytes(stages);
 }
 
+// Tile widths: 1-CTA variants 256; pairs 128, 256 or 512 (stream-K 128 or 256).
 // `tile_n` 0 picks the variant's default width (256).
 int variant_shape(int variant, int tile_n, VariantShape* vs) {
-  if (tile_n != 0 && tile_n != 256 && tile_n != 512) return B200_ERR_INVALID_ARG;
-  const bool wide = (tile_n == 512);
+  if (tile_n != 0 && tile_n != 128 && tile_n != 256 && tile_n != 512) return B200_ERR_INVALID_ARG;
+  const int tn = tile_n ? tile_n : 256;
   switch (variant) {
     case B200_VARIANT_1CTA:
     case B200_VARIANT_PERSISTENT:
-      if (wide) return B200_ERR_INVALID_ARG;
-      fill_shape<1, b200::SCHED_STATIC, 1>(vs);
+      if (tn != 256) return B200_ERR_INVALID_ARG;
+      fill_shape<1, b200::SCHED_STATIC, 256>(vs);
       break;
     case B200_VARIANT_CLC:
-      if (wide) return B200_ERR_INVALID_ARG;
-      fill_shape<1, b200::SCHED_CLC, 1>(vs);
+      if (tn != 256) return B200_ERR_INVALID_ARG;
+      fill_shape<1, b200::SCHED_CLC, 256>(vs);
       break;
     case B200_VARIANT_2CTA:
-      if (wide) fill_shape<2, b200::SCHED_STATIC, 2>(vs);
-      else fill_shape<2, b200::SCHED_STATIC, 1>(vs);
+      if (tn == 128) fill_shape<2, b200::SCHED_STATIC, 128>(vs);
+      else if (tn == 256) fill_shape<2, b200::SCHED_STATIC, 256>(vs);
+      else fill_shape<2, b200::SCHED_STATIC, 512>(vs);
       break;
     case B200_VARIANT_2CTA_CLC:
-      if (wide) fill_shape<2, b200::SCHED_CLC, 2>(vs);
-      else fill_shape<2, b200::SCHED_CLC, 1>(vs);
+      if (tn == 128) fill_shape<2, b200::SCHED_CLC, 128>(vs);
+      else if (tn == 256) fill_shape<2, b200::SCHED_CLC, 256>(vs);
+      else fill_shape<2, b200::SCHED_CLC, 512>(vs);
       break;
     case B200_VARIANT_2CTA_STREAMK:
-      if (wide) return B200_ERR_INVALID_ARG;
-      fill_shape<2, b200::SCHED_STREAMK, 1>(vs);
-      break;
-    case B200_VARIANT_2CTA_SHARE:
-      if (tile_n == 256) return B200_ERR_INVALID_ARG;  // built for 256x512 tiles only
-      fill_shape<2, b200::SCHED_SHARE, 2>(vs);
+      if (tn == 512) return B200_ERR_INVALID_ARG;
+      if (tn == 128) fill_shape<2, b200::SCHED_STREAMK, 128>(vs);
+      else fill_shape<2, b200::SCHED_STREAMK, 256>(vs);
       break;
     default: return B200_ERR_INVALID_ARG;
   }
@@ -202,50 +230,64 @@ int variant_shape(int variant, int tile_n, VariantShape* vs) {
 }
 
 uint32_t variant_smem(const VariantShape& vs, uint32_t stages) {
-  if (vs.cg == 1) return shape_smem<1, 0, 1>(stages);
-  if (vs.nh == 1) return shape_smem<2, 0, 1>(stages);
-  return shape_smem<2, 0, 2>(stages);
+  if (vs.cg == 1) return shape_smem<1, 256>(stages);
+  if (vs.tn == 128) return shape_smem<2, 128>(stages);
+  if (vs.tn == 256) return shape_smem<2, 256>(stages);
+  return shape_smem<2, 512>(stages);
 }
 
-// C columns per tile for a pair variant when the caller leaves tile_n = 0: the
-// 256x512 tile cuts operand traffic by a quarter (less power, so a
-// higher clock under the power cap) but its accumulator is single-buffered, so it
-// only pays when the main loop is long (K >= 4096) and there are at least two
-// waves of wide tiles. Measured, one launch at 8192^3: f16 711 us (512) vs 729 us
-// (256), e4m3 equal; sustained under the power cap: f16 1282 vs 1217 TFLOPS, e4m3
-// 2489 vs 2464 (8192^3) and 2497 vs 2438 (16384^3), with less energy per GEMM.
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// C columns per tile for a pair variant when the caller leaves tile_n = 0. Chosen from
+// launch-time sweeps on B200 (bench.py --mode sweep; medians of 30 launches):
+//   512: the 256x512 tile cuts operand traffic by a quarter (less power, so a higher
+//        clock under the power cap) but its accumulator is single-buffered, so it only
+//        pays with a long main loop (K >= 4096) and at least one full wave of wide
+//        tiles: 4096^3 f16 1366 vs 1310 TFLOPS (256-wide), 8192^3 f16 711 vs 729 us per
+//        launch; 2048x2048x8192 (32 wide tiles) 795 vs 1234.
+//   128: the 256x128 tile moves 1.5x the operand bytes per flop into each SM, and the
+//        SMs' L2 ingress caps it at ~0.7x the per-column rate of 256-wide tiles (8192^2
+//        x 1024 f16: 865 vs 1265 TFLOPS), so it is taken only where 256-wide tiles
+//        would leave more than half of the pairs idle: 2048x1024x4096 f16 593 vs 555,
+//        e4m3 915 vs 823; 2048x1024x8192 f16 756 vs 696. This is the reference's open
+//        BN=64/128 choice (docs/notes/08_persistent.md:213) decided by wave count.
+//   stream-K: 128 (its splits then cover twice the pairs per tile column): 1024x1024x
+//        16384 f16 723 vs 666 TFLOPS (256-wide), 512x1024x8192 f16 319 vs 181.
 int pick_tile_n(const B200GemmArgs* a, int variant, int sms) {
-  if (variant == B200_VARIANT_2CTA_SHARE) return 512;
-  if (variant != B200_VARIANT_2CTA && variant != B200_VARIANT_2CTA_CLC) return 256;
-  if (a->K < 4096) return 256;
-  const int64_t wide_tiles = ((a->M + 255) / 256) * ((a->N + 511) / 512);
-  return wide_tiles >= sms ? 512 : 256;
+  if (variant != B200_VARIANT_2CTA && variant != B200_VARIANT_2CTA_CLC &&
+      variant != B200_VARIANT_2CTA_STREAMK)
+    return 256;
+  if (variant == B200_VARIANT_2CTA_STREAMK) return 128;
+  const int64_t pairs = sms / 2;
+  if (a->K >= 4096 && ceil_div(a->M, 256) * ceil_div(a->N, 512) >= pairs) return 512;
+  if (ceil_div(a->M, 256) * ceil_div(a->N, 256) * 2 <= pairs) return 128;
+  return 256;
 }
 
 int pick_variant(const B200GemmArgs* a, int sms, bool allow_workspace) {
-  const int64_t pair_tiles = ((a->M + 255) / 256) * ((a->N + 255) / 256);
-  const int64_t cta_tiles = ((a->M + 127) / 128) * ((a->N + 255) / 256);
   const int64_t pairs = sms / 2;
+  const int64_t pair_tiles = ceil_div(a->M, 256) * ceil_div(a->N, 256);
+  const int64_t cta_tiles = ceil_div(a->M, 128) * ceil_div(a->N, 256);
   // A pair computes the same 256 x 256 area per SM-pair-step as two 1-CTA tiles while
   // reading each B row once per pair, so it wins whenever it needs no more waves than
   // the 1-CTA tiling (it needs more only when M rounds up badly, e.g. M = 384).
-  const int64_t pair_waves = (pair_tiles + pairs - 1) / pairs;
-  const int64_t cta_waves = (cta_tiles + sms - 1) / sms;
+  const int64_t pair_waves = ceil_div(pair_tiles, pairs);
+  const int64_t cta_waves = ceil_div(cta_tiles, sms);
   if (a->M >= 256 && pair_waves <= cta_waves) {
-    // Stream-K only when the static pair schedule would leave three quarters of the
-    // pairs idle and K is long: each split tile costs a 128 KB fp32 partial written
-    // and read back through L2 per CTA, a few microseconds that only a long K loop
-    // repays (measured: 1024x1024x8192 f16 +23%, 1024x1024x16384 f16 +71% and e4m3
-    // +15%; 1024x1024x8192 e4m3, 2048^3 and 256x16384x8192 slower than static).
-    if (allow_workspace && pair_tiles * 4 <= pairs) {
-      const int64_t stage_k = (a->ab_dtype == B200_DT_E4M3) ? 256 : 128;
-      if ((a->K + stage_k - 1) / stage_k >= 48) return B200_VARIANT_2CTA_STREAMK;
-    }
-    // More than one wave: the persistent pairs take their next tiles from
-    // cluster-launch-control work stealing (even with the static order's speed:
-    // 8192^3 sustained f16 1302 vs 1293 TFLOPS, e4m3 2597 vs 2580, and it adapts to
-    // SMs that run slower or are shared). One wave needs no scheduler at all.
-    if (pair_tiles > pairs) return B200_VARIANT_2CTA_CLC;
+    // Stream-K only when 256-wide pair tiles would leave three quarters of the pairs
+    // idle and K is long (>= 6144): each split tile costs an fp32 partial written and
+    // read back through L2 per CTA, a few microseconds that only a long K loop repays
+    // (measured, 128-wide stream-K: 1024x1024x8192 f16 518 TFLOPS vs 396 for the best
+    // static tiling, e4m3 687 vs 636; 512x1024x8192 f16 319 vs 198, e4m3 375 vs 318).
+    if (allow_workspace && pair_tiles * 4 <= pairs && a->K >= 6144) return B200_VARIANT_2CTA_STREAMK;
+    // More than one wave (at the width pick_tile_n will choose): the persistent pairs
+    // take their next tiles from cluster-launch-control work stealing (even with the
+    // static order's speed: 8192^3 sustained f16 1302 vs 1293 TFLOPS, e4m3 2597 vs
+    // 2580, and it adapts to SMs that run slower or are shared). One wave needs no
+    // scheduler at all.
+    const int tn = pick_tile_n(a, B200_VARIANT_2CTA, sms);
+    const int64_t tiles = ceil_div(a->M, 256) * ceil_div(a->N, tn);
+    if (tiles > pairs) return B200_VARIANT_2CTA_CLC;
     return B200_VARIANT_2CTA;
   }
   return cta_tiles > sms ? B200_VARIANT_PERSISTENT : B200_VARIANT_1CTA;
@@ -295,8 +337,10 @@ int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status,
   CUtensorMap& tC = out->tC;
   rc = encode_2d(&tA, a.A, a.ab_dtype, uint64_t(a.M), uint64_t(a.K), uint64_t(a.lda), 128u, bk);
   if (rc != B200_OK) return rc;
+  // B box: the rows of one MMA's N that this CTA loads (a pair splits them)
+  const uint32_t mma_n = vs.tile_n > 256u ? 256u : vs.tile_n;
   rc = encode_2d(&tB, a.B, a.ab_dtype, uint64_t(a.N), uint64_t(a.K), uint64_t(a.ldb),
-                 256u / uint32_t(vs.cg), bk);
+                 mma_n / uint32_t(vs.cg), bk);
   if (rc != B200_OK) return rc;
   rc = encode_2d(&tC, a.C, a.c_dtype, uint64_t(a.M), uint64_t(a.N), uint64_t(a.ldc), 32u, cd_cols);
   if (rc != B200_OK) return rc;
@@ -310,16 +354,15 @@ int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status,
   const uint64_t tiles = uint64_t(kp.m_tiles) * kp.n_tiles;
   if (tiles > 0x7fffffffull / 4) return B200_ERR_SHAPE;
   kp.num_tiles = uint32_t(tiles);
-  // B sharing pairs tiles into super-tiles of two block-rows (see tile_coords)
-  if (variant == B200_VARIANT_2CTA_SHARE) kp.num_tiles = 2u * ((kp.m_tiles + 1u) / 2u) * kp.n_tiles;
   kp.k_blocks = uint32_t((a.K + stage_k - 1) / stage_k);
   kp.stages = stages;
-  kp.group_m = a.group_m ? uint32_t(a.group_m) : uint32_t(vs.nh == 2 ? kDefaultGroupMWide : kDefaultGroupM);
+  kp.group_m = a.group_m ? uint32_t(a.group_m) : uint32_t(vs.tn == 512 ? kDefaultGroupMWide : kDefaultGroupM);
   kp.fault_inject = a.fault_inject ? 1u : 0u;
   kp.scale_a = a.scale_a;
   kp.scale_b = a.scale_b;
   kp.status = status;
   kp.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kDefaultWaitNs;
+  kp.l2_policy = kL2Policy;
   if (gather) {
     kp.gather = static_cast<const uint8_t*>(gather->dst);
     kp.gather_mode = gather->mode;
@@ -340,13 +383,6 @@ int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status,
       break;
     }
     case B200_VARIANT_2CTA_CLC: grid = 2u * kp.num_tiles; break;
-    case B200_VARIANT_2CTA_SHARE: {
-      // an even number of pairs keeps the two pairs of a 4-CTA cluster on the two
-      // halves of one super-tile at every step (the tile count is even as well)
-      const uint32_t pairs = (n_sms / 2) & ~1u;
-      grid = 2u * (kp.num_tiles < pairs ? kp.num_tiles : pairs);
-      break;
-    }
     case B200_VARIANT_2CTA_STREAMK: {
       // every pair must be resident at once (a split tile's last owner waits for
       // the partial sums of the earlier owners), so at most one pair per SM pair
@@ -369,7 +405,7 @@ int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status,
   out->cd = a.c_dtype;
   out->cg = vs.cg;
   out->sched = vs.sched;
-  out->nh = vs.nh;
+  out->tn = vs.tn;
   return B200_OK;
 }
 
@@ -380,11 +416,6 @@ int gemm_launch_prepared(Prepared& pr, cudaStream_t stream) {
     cudaError_t e = cudaMemset2DAsync(pr.c, pr.c_pitch, 0, pr.c_width, pr.c_height, stream);
     return e == cudaSuccess ? B200_OK : B200_ERR_CUDA;
   }
-  if (pr.streamk) {
-    uint32_t ep = g_sk_epoch[pr.dev].fetch_add(1) + 1;
-    if (ep == 0) ep = g_sk_epoch[pr.dev].fetch_add(1) + 1;  // 0 is the flags' initial value
-    pr.kp.sk_epoch = ep;
-  }
   LaunchPlan lp;
   lp.a = &pr.tA;
   lp.b = &pr.tB;
@@ -393,12 +424,38 @@ int gemm_launch_prepared(Prepared& pr, cudaStream_t stream) {
   lp.grid = pr.grid;
   lp.stream = stream;
   lp.smem = pr.smem;
+  auto launch = [&]() -> cudaError_t {
+    switch (pr.ab) {
+      case B200_DT_F16: return b200::launch_f16(pr.cd, pr.cg, pr.sched, pr.tn, lp);
+      case B200_DT_BF16: return b200::launch_bf16(pr.cd, pr.cg, pr.sched, pr.tn, lp);
+      default: return b200::launch_e4m3(pr.cd, pr.cg, pr.sched, pr.tn, lp);
+    }
+  };
 
   cudaError_t e;
-  switch (pr.ab) {
-    case B200_DT_F16: e = b200::launch_f16(pr.cd, pr.cg, pr.sched, pr.nh, lp); break;
-    case B200_DT_BF16: e = b200::launch_bf16(pr.cd, pr.cg, pr.sched, pr.nh, lp); break;
-    default: e = b200::launch_e4m3(pr.cd, pr.cg, pr.sched, pr.nh, lp); break;
+  if (pr.streamk) {
+    // One workspace per device: order this launch after the previous stream-K launch
+    // when that one went to another stream (inside a stream capture the caller's
+    // graph edges order the launches, and nothing is recorded).
+    std::lock_guard<std::mutex> lk(g_sk_mu);
+    const int dev = pr.dev;
+    uint32_t ep = g_sk_epoch[dev].fetch_add(1) + 1;
+    if (ep == 0) ep = g_sk_epoch[dev].fetch_add(1) + 1;  // 0 is the flags' initial value
+    lp.kp.sk_epoch = ep;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) return B200_ERR_CUDA;
+    const bool capturing = cs != cudaStreamCaptureStatusNone;
+    if (!capturing && g_sk_recorded[dev] && g_sk_last_stream[dev] != stream) {
+      if (cudaStreamWaitEvent(stream, g_sk_event[dev], 0) != cudaSuccess) return B200_ERR_CUDA;
+    }
+    e = launch();
+    if (e == cudaSuccess && !capturing) {
+      if (cudaEventRecord(g_sk_event[dev], stream) != cudaSuccess) return B200_ERR_CUDA;
+      g_sk_recorded[dev] = true;
+      g_sk_last_stream[dev] = stream;
+    }
+  } else {
+    e = launch();
   }
   if (e == cudaErrorNotSupported) return B200_ERR_UNSUPPORTED;
   if (e != cudaSuccess) {
@@ -460,13 +517,13 @@ static int validate(const B200GemmArgs* a) {
     return B200_ERR_INVALID_ARG;
   if (a->c_dtype != B200_DT_F16 && a->c_dtype != B200_DT_BF16 && a->c_dtype != B200_DT_F32)
     return B200_ERR_INVALID_ARG;
-  if (a->variant < B200_VARIANT_AUTO || a->variant > B200_VARIANT_2CTA_SHARE) return B200_ERR_INVALID_ARG;
+  if (a->variant < B200_VARIANT_AUTO || a->variant > B200_VARIANT_2CTA_STREAMK) return B200_ERR_INVALID_ARG;
   if (a->M < 0 || a->N < 0 || a->K < 0) return B200_ERR_SHAPE;
   // TMA coordinates are int32 and the tile counters are uint32.
   const int64_t lim = (int64_t(1) << 31) - 1;
   if (a->M > lim || a->N > lim || a->K > lim) return B200_ERR_SHAPE;
   if (a->group_m < 0 || a->stages < 0 || a->reserved != 0) return B200_ERR_INVALID_ARG;
-  if (a->tile_n != 0 && a->tile_n != 256 && a->tile_n != 512) return B200_ERR_INVALID_ARG;
+  if (a->tile_n != 0 && a->tile_n != 128 && a->tile_n != 256 && a->tile_n != 512) return B200_ERR_INVALID_ARG;
   if (a->M == 0 || a->N == 0) return B200_OK;
   if (a->ldc < a->N) return B200_ERR_SHAPE;
   if (!a->C) return B200_ERR_INVALID_ARG;
@@ -497,6 +554,19 @@ int b200_gemm_pick_variant(const B200GemmArgs* args) {
   return pick_variant(args, g_sm_count[dev], true);
 }
 
+int b200_gemm_pick_config(const B200GemmArgs* args, int32_t* variant, int32_t* tile_n) {
+  int rc = validate(args);
+  if (rc != B200_OK) return rc;
+  if (!variant || !tile_n) return B200_ERR_INVALID_ARG;
+  int dev = 0;
+  rc = device_setup(&dev);
+  if (rc != B200_OK) return rc;
+  const int v = args->variant == B200_VARIANT_AUTO ? pick_variant(args, g_sm_count[dev], true) : args->variant;
+  *variant = v;
+  *tile_n = args->tile_n ? args->tile_n : pick_tile_n(args, v, g_sm_count[dev]);
+  return B200_OK;
+}
+
 int b200_gemm(const B200GemmArgs* args, void* stream_v) {
   int rc = validate(args);
   if (rc != B200_OK) return rc;
@@ -506,7 +576,7 @@ int b200_gemm(const B200GemmArgs* args, void* stream_v) {
   int dev = 0;
   rc = device_setup(&dev);
   if (rc != B200_OK) return rc;
-  return b200::gemm_launch_impl(a, stream, g_sm_count[dev], g_cc_major[dev], g_status[dev]);
+  return b200::gemm_launch_impl(a, stream, g_sm_count[dev], g_cc_major[dev], status_word(dev));
 }
 
 struct B200GemmPlan {
@@ -526,7 +596,7 @@ int b200_gemm_plan_create(const B200GemmArgs* args, B200GemmPlan** plan) {
   if (!p) return B200_ERR_CUDA;
   p->empty = args->M == 0 || args->N == 0;
   if (!p->empty) {
-    rc = b200::gemm_prepare(*args, g_sm_count[dev], g_cc_major[dev], g_status[dev], true, nullptr, &p->pr);
+    rc = b200::gemm_prepare(*args, g_sm_count[dev], g_cc_major[dev], status_word(dev), true, nullptr, &p->pr);
     if (rc != B200_OK) {
       delete p;
       return rc;
@@ -563,24 +633,13 @@ int b200_gemm_allgather(const B200GemmArgs* args, const void* dst, int32_t mode,
   int dev = 0;
   rc = device_setup(&dev);
   if (rc != B200_OK) return rc;
-  // Static schedules only. With the cluster-launch-control schedule, multicast
-  // (multimem) stores from the epilogue made launches stall intermittently until the
-  // kernel's 1 s bounded waits fired (measured on 2 GPUs; the same launches with peer
-  // stores, or with the static schedule, never did), so AUTO maps to the static
-  // counterpart and an explicit CLC or stream-K request is refused.
-  B200GemmArgs a2 = a;
-  if (a2.variant == B200_VARIANT_AUTO) {
-    int v = pick_variant(&a2, g_sm_count[dev], /*allow_workspace=*/false);
-    if (v == B200_VARIANT_2CTA_CLC) v = B200_VARIANT_2CTA;
-    if (v == B200_VARIANT_CLC) v = B200_VARIANT_PERSISTENT;
-    a2.variant = v;
-  } else if (a2.variant != B200_VARIANT_1CTA && a2.variant != B200_VARIANT_PERSISTENT &&
-             a2.variant != B200_VARIANT_2CTA) {
-    return B200_ERR_UNSUPPORTED;
-  }
+  // Every schedule but stream-K (whose partial-tile workspace this entry point does
+  // not take): AUTO resolves as for b200_gemm without the workspace.
+  if (a.variant == B200_VARIANT_2CTA_STREAMK) return B200_ERR_UNSUPPORTED;
+  const B200GemmArgs& a2 = a;
   b200::GatherSpec g{dst, uint32_t(mode), uint32_t(mode == B200_GATHER_PEERS ? npeers : 0), uint64_t(ldg),
                      uint64_t(col_off)};
-  return b200::gemm_launch_impl(a2, stream, g_sm_count[dev], g_cc_major[dev], g_status[dev], false, &g);
+  return b200::gemm_launch_impl(a2, stream, g_sm_count[dev], g_cc_major[dev], status_word(dev), false, &g);
 }
 
 int b200_gemm_status(void* stream_v, int clear, uint32_t* bits) {
@@ -590,10 +649,10 @@ int b200_gemm_status(void* stream_v, int clear, uint32_t* bits) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (cudaStreamSynchronize(stream) != cudaSuccess) return B200_ERR_CUDA;
   uint32_t v = 0;
-  if (cudaMemcpy(&v, g_status[dev], sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess)
+  if (cudaMemcpy(&v, status_word(dev), sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess)
     return B200_ERR_CUDA;
   if (clear && v) {
-    if (cudaMemset(g_status[dev], 0, sizeof(uint32_t)) != cudaSuccess) return B200_ERR_CUDA;
+    if (cudaMemset(status_word(dev), 0, sizeof(uint32_t)) != cudaSuccess) return B200_ERR_CUDA;
   }
   if (bits) *bits = v;
   return v ? B200_ERR_DEVICE_TIMEOUT : B200_OK;

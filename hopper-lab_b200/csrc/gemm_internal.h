@@ -42,7 +42,7 @@ struct Prepared {
   alignas(64) CUtensorMap tC;
   KParams kp;
   uint32_t grid, smem;
-  int ab, cd, cg, sched, nh;
+  int ab, cd, cg, sched, tn;
   int dev;
   bool streamk;      // takes a fresh workspace epoch per launch
   bool memset_only;  // K == 0: C = 0

@@ -17,10 +17,10 @@ struct LaunchPlan {
   cudaStream_t stream;
 };
 
-template <int AB, int CD, int CG, int SCHED, int NH>
+template <int AB, int CD, int CG, int SCHED, int TN>
 cudaError_t launch_gemm(const LaunchPlan& lp) {
-  using Cfg = GemmCfg<AB, CD, CG, SCHED, NH>;
-  auto kern = gemm_tcgen05_kernel<AB, CD, CG, SCHED, NH>;
+  using Cfg = GemmCfg<AB, CD, CG, SCHED, TN>;
+  auto kern = gemm_tcgen05_kernel<AB, CD, CG, SCHED, TN>;
   // The opt-in shared-memory size is a per-function, per-device attribute.
   static int configured[64] = {0};
   int dev = 0;
@@ -38,7 +38,7 @@ cudaError_t launch_gemm(const LaunchPlan& lp) {
   cfg.blockDim = dim3(Cfg::NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = lp.smem;
   cfg.stream = lp.stream;
-  cudaLaunchAttribute attr[3];
+  cudaLaunchAttribute attr[2];
   // programmatic dependent launch: the kernel waits (griddepcontrol.wait) for the
   // previous kernel of the stream before touching global memory, so its launch and
   // set-up may overlap that kernel's tail (2048^3 back to back: 18.5 -> 16.5 us)
@@ -52,15 +52,6 @@ cudaError_t launch_gemm(const LaunchPlan& lp) {
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     cfg.numAttrs = 2;
-    if (SCHED == SCHED_SHARE && lp.grid % 4 == 0) {
-      // two pairs per cluster where a GPC has room, plain pairs elsewhere (on B200:
-      // 33 clusters of 4 and 8 of 2 for a 148-CTA grid)
-      attr[2].id = cudaLaunchAttributePreferredClusterDimension;
-      attr[2].val.preferredClusterDim.x = 4;
-      attr[2].val.preferredClusterDim.y = 1;
-      attr[2].val.preferredClusterDim.z = 1;
-      cfg.numAttrs = 3;
-    }
   }
   if (SCHED == SCHED_STREAMK) {
     // A split tile's last owner waits for the earlier owners' partial sums, so the
@@ -79,31 +70,36 @@ cudaError_t launch_gemm(const LaunchPlan& lp) {
 }
 
 // One dispatch entry per A/B type — defined in the instantiation units. Selects
-// the instantiation for (C type, CTAs per tile, schedule, N-halves per tile).
-cudaError_t launch_f16(int cd, int cg, int sched, int nh, const LaunchPlan& lp);
-cudaError_t launch_bf16(int cd, int cg, int sched, int nh, const LaunchPlan& lp);
-cudaError_t launch_e4m3(int cd, int cg, int sched, int nh, const LaunchPlan& lp);
+// the instantiation for (C type, CTAs per tile, schedule, tile width).
+cudaError_t launch_f16(int cd, int cg, int sched, int tn, const LaunchPlan& lp);
+cudaError_t launch_bf16(int cd, int cg, int sched, int tn, const LaunchPlan& lp);
+cudaError_t launch_e4m3(int cd, int cg, int sched, int tn, const LaunchPlan& lp);
 
-#define B200_DISPATCH_CD(AB, CG, SCHED, NH)                                              \
+#define B200_DISPATCH_CD(AB, CG, SCHED, TN)                                              \
   do {                                                                                   \
-    if (cd == DT_F16) return launch_gemm<AB, DT_F16, CG, SCHED, NH>(lp);                 \
-    if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, CG, SCHED, NH>(lp);               \
-    if (cd == DT_F32) return launch_gemm<AB, DT_F32, CG, SCHED, NH>(lp);                 \
+    if (cd == DT_F16) return launch_gemm<AB, DT_F16, CG, SCHED, TN>(lp);                 \
+    if (cd == DT_BF16) return launch_gemm<AB, DT_BF16, CG, SCHED, TN>(lp);               \
+    if (cd == DT_F32) return launch_gemm<AB, DT_F32, CG, SCHED, TN>(lp);                 \
   } while (0)
 
+// Built: 1-CTA 128x256 (static, CLC); pairs 256x128 and 256x256 (static, CLC,
+// stream-K) and 256x512 (static, CLC).
 #define B200_DEFINE_DISPATCH(NAME, AB)                                                  \
-  cudaError_t NAME(int cd, int cg, int sched, int nh, const LaunchPlan& lp) {           \
-    if (cg == 1 && nh == 1) {                                                            \
-      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 1, SCHED_STATIC, 1);               \
-      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 1, SCHED_CLC, 1);                     \
-    } else if (cg == 2 && nh == 1) {                                                     \
-      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 1);               \
-      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 1);                     \
-      if (sched == SCHED_STREAMK) B200_DISPATCH_CD(AB, 2, SCHED_STREAMK, 1);             \
-    } else if (cg == 2 && nh == 2) {                                                     \
-      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 2);               \
-      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 2);                     \
-      if (sched == SCHED_SHARE) B200_DISPATCH_CD(AB, 2, SCHED_SHARE, 2);                 \
+  cudaError_t NAME(int cd, int cg, int sched, int tn, const LaunchPlan& lp) {           \
+    if (cg == 1 && tn == 256) {                                                          \
+      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 1, SCHED_STATIC, 256);             \
+      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 1, SCHED_CLC, 256);                   \
+    } else if (cg == 2 && tn == 128) {                                                   \
+      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 128);             \
+      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 128);                   \
+      if (sched == SCHED_STREAMK) B200_DISPATCH_CD(AB, 2, SCHED_STREAMK, 128);           \
+    } else if (cg == 2 && tn == 256) {                                                   \
+      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 256);             \
+      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 256);                   \
+      if (sched == SCHED_STREAMK) B200_DISPATCH_CD(AB, 2, SCHED_STREAMK, 256);           \
+    } else if (cg == 2 && tn == 512) {                                                   \
+      if (sched == SCHED_STATIC) B200_DISPATCH_CD(AB, 2, SCHED_STATIC, 512);             \
+      if (sched == SCHED_CLC) B200_DISPATCH_CD(AB, 2, SCHED_CLC, 512);                   \
     }                                                                                    \
     return cudaErrorNotSupported;                                                        \
   }

@@ -16,31 +16,29 @@
 //                    per-tensor fp32 scales fused in the epilogue
 //   gemm_fp8_persist (src/08_persistent/gemm_fp8_persist.cu:68) -> SCHED_STATIC
 //                    (grid = resident CTAs, tile += grid, group-M order)
-//   gemm_fp8_bn128   (src/08_persistent/gemm_fp8_bn128.cu:73, dynamic queue)
+//   gemm_fp8_bn128   (src/08_persistent/gemm_fp8_bn128.cu:73, dynamic queue, BN=128)
 //                    -> SCHED_CLC: hardware cluster-launch-control work stealing
-//                    replaces the global atomic tile counter
-//   gemm_ws_cluster's shared operand across clusters -> SCHED_SHARE: two CTA pairs in
-//                    one 4-CTA cluster compute vertically adjacent 256 x 512 tiles and
-//                    share B: each CTA loads half of its B rows and copies them into the
-//                    other pair's CTA over DSMEM (a shared::cta -> shared::cluster bulk
-//                    copy, no multicast load), a third less L2 traffic per flop
+//                    replaces the global atomic tile counter; TN = 128 is the narrow
+//                    tile (256 x 128 per pair) for problems whose 256-wide tiles
+//                    leave pairs idle
 //
 // CTA = 384 threads, 12 warps:
 //   warp 0      TMA producer (one lane): A/B k-blocks into an S-stage smem ring
-//               (one 128-byte K atom per stage for 1-CTA tiles, two for pairs)
+//               (one 128-byte K atom per stage for 1-CTA and 512-wide tiles, two
+//               for the other pair tiles)
 //   warp 1      TMEM owner + MMA issuer (one lane of the leader CTA)
-//   warp 2      CLC scheduler (one lane of the leader CTA; SCHED_CLC only);
-//               SCHED_SHARE: B relay (tells the pair leader a stage's B rows are in)
-//   warp 3      SCHED_SHARE: B forwarder (copies this CTA's B rows to the other pair);
-//               otherwise idle
+//   warp 2      CLC scheduler (one lane of the leader CTA; SCHED_CLC only)
+//   warp 3      idle
 //   warps 4-11  epilogue: TMEM -> registers -> (scale, narrow) -> swizzled smem ->
 //               TMA store; warp 4+4e+q drains TMEM lanes 32q..32q+31, columns of half
-//               e of each 256-column slot
-// TMEM holds two 256-column fp32 slots. A tile of NH = 1 half (BN = 256) uses one
-// slot, so the epilogue of tile t overlaps the main loop of tile t+1. A pair tile of
-// NH = 2 halves (256 x 512, two N=256 MMAs per K-step sharing the A tiles, 25% less
-// operand traffic per flop) uses both slots; the epilogue releases each slot as
-// soon as it is drained, and the next tile's first MMAs into that slot start then.
+//               e of each accumulator slot
+// TN is the tile width (C columns per tile): 128, 256 or 512. One MMA is
+// MMA_N = min(TN, 256) wide and TMEM holds two MMA_N-column fp32 slots. A tile of one
+// MMA width (TN = 128 or 256) uses one slot, so the epilogue of tile t overlaps the
+// main loop of tile t+1. A pair tile of TN = 512 (two N=256 MMAs per K-step sharing
+// the A tiles, 25% less operand traffic per flop) uses both slots; the epilogue
+// releases each slot as soon as it is drained, and the next tile's first MMAs into
+// that slot start then.
 #pragma once
 
 #include "sm100_ptx.cuh"
@@ -48,7 +46,7 @@
 namespace b200 {
 
 enum : int { DT_F16 = 0, DT_BF16 = 1, DT_E4M3 = 2, DT_F32 = 3 };
-enum : int { SCHED_STATIC = 0, SCHED_CLC = 1, SCHED_STREAMK = 2, SCHED_SHARE = 3 };
+enum : int { SCHED_STATIC = 0, SCHED_CLC = 1, SCHED_STREAMK = 2 };
 
 // Bits OR-ed into the device status word when a bounded wait gives up.
 enum : uint32_t {
@@ -59,15 +57,14 @@ enum : uint32_t {
   ST_SCHED = 1u << 4,
   ST_DRAIN = 1u << 5,
   ST_STREAMK = 1u << 6,
-  ST_SHARE = 1u << 7,
   ST_ABORTED = 1u << 31,
 };
 
 struct KParams {
   uint32_t M, N, K;
   uint32_t m_tiles;    // ceil(M / (128*CG))
-  uint32_t n_tiles;    // ceil(N / BN)
-  uint32_t num_tiles;  // m_tiles * n_tiles (SCHED_SHARE: 2 * ceil(m_tiles / 2) * n_tiles)
+  uint32_t n_tiles;    // ceil(N / TN)
+  uint32_t num_tiles;  // m_tiles * n_tiles
   uint32_t k_blocks;   // ceil(K / BK)
   uint32_t stages;     // smem ring depth (runtime, ≤ the kernel's maximum)
   uint32_t group_m;    // group-M swizzle width (≥ 1)
@@ -76,7 +73,11 @@ struct KParams {
   const float* scale_b;
   uint32_t* status;       // device status word, may be null
   uint64_t wait_ns;       // bound of every mbarrier wait
-  // SCHED_STREAMK only: fp32 partial-tile workspace (one 128 x 256 region per CTA
+  // L2 cache policies: bit 0 A loads evict_last (A panels are reused by every wave of a
+  // group-M group), bit 1 B loads evict_first (a B panel's reuse is within one wave),
+  // bit 2 C stores evict_first (C is never read back); 0 = evict_normal everywhere
+  uint32_t l2_policy;
+  // SCHED_STREAMK only: fp32 partial-tile workspace (one 128 x MMA_N region per CTA
   // slot), per-slot ready flags, and this launch's epoch (the value a ready flag
   // holds; flags never need resetting between launches)
   float* sk_work;
@@ -119,23 +120,24 @@ __host__ __device__ inline void tile_to_bmn(uint32_t tile, uint32_t num_bm, uint
   bn = t / gsize;
 }
 
-template <int AB, int CD, int CG, int SCHED, int NH>
+template <int AB, int CD, int CG, int SCHED, int TN>
 struct GemmCfg {
   static constexpr int BM = 128;                       // rows of C per CTA
-  static constexpr int MMA_N = 256;                    // N of one tcgen05.mma
-  static constexpr int BN = MMA_N * NH;                // columns of C per tile
+  static constexpr int MMA_N = TN > 256 ? 256 : TN;    // N of one tcgen05.mma
+  static constexpr int NH = TN / MMA_N;                // MMAs (accumulator slots) per tile
+  static constexpr int BN = TN;                        // columns of C per tile
   static constexpr int KIND = (AB == DT_E4M3) ? 1 : 0; // 0 kind::f16, 1 kind::f8f6f4
   static constexpr int AB_BYTES = (AB == DT_E4M3) ? 1 : 2;
-  // One 128-byte swizzle atom of K per TMA box. A pair stage carries two atoms:
-  // one commit / barrier round trip per 8 MMAs instead of 4 keeps the tensor pipe
-  // busy (the per-stage commit costs tensor-pipe time); 1-CTA stages are already
-  // 48 KB and keep one atom so that four of them fit.
+  // One 128-byte swizzle atom of K per TMA box. A pair stage of one MMA width carries
+  // two atoms: one commit / barrier round trip per 8 MMAs instead of 4 keeps the
+  // tensor pipe busy (the per-stage commit costs tensor-pipe time); 1-CTA stages
+  // and 512-wide pair stages are already 48 KB and keep one atom so that four fit.
   static constexpr int ATOMS = (CG == 2 && NH == 1) ? 2 : 1;
   static constexpr int ATOM_K = 128 / AB_BYTES;        // elements of K per atom
   static constexpr int BK = ATOMS * ATOM_K;            // elements of K per stage
   static constexpr int KSTEPS = 4 * ATOMS;             // 32-byte MMA K-steps per stage
-  static constexpr int B_HALF_ROWS = MMA_N / CG;       // rows of B per CTA per N-half
-  static constexpr uint32_t B_HALF = B_HALF_ROWS * 128; // bytes of one half in one atom
+  static constexpr int B_HALF_ROWS = MMA_N / CG;       // rows of B per CTA per MMA
+  static constexpr uint32_t B_HALF = B_HALF_ROWS * 128; // bytes of one MMA's B in one atom
   static constexpr uint32_t A_ATOM = BM * 128;         // bytes
   static constexpr uint32_t B_ATOM = NH * B_HALF;
   static constexpr uint32_t A_STAGE = ATOMS * A_ATOM;
@@ -143,19 +145,20 @@ struct GemmCfg {
   static constexpr uint32_t STAGE = A_STAGE + B_STAGE;
   static constexpr int CD_BYTES = (CD == DT_F32) ? 4 : 2;
   static constexpr int EPI_COLS = 128 / CD_BYTES;      // C columns per 128-byte chunk
-  static constexpr int EPI_CHUNKS = MMA_N / EPI_COLS; // per 256-column slot
+  static constexpr int EPI_CHUNKS = MMA_N / EPI_COLS; // per accumulator slot
   static constexpr uint32_t EPI_BUF = 32 * 128;        // 32 rows × 128 bytes
   // Eight epilogue warps: warp 4 + 4e + q drains TMEM lane quarter q, column half e
-  // of each 256-column slot, staging through one 4 KB buffer of its own.
+  // of each slot, staging through one 4 KB buffer of its own.
   static constexpr int EPI_WARPS = 8;
   static constexpr int EPI_CHUNKS_PER_WARP = EPI_CHUNKS / 2;
+  static constexpr int EPI_VALS = EPI_CHUNKS_PER_WARP * EPI_COLS;  // fp32 values per thread
   static constexpr uint32_t EPI_BYTES = EPI_WARPS * EPI_BUF;
-  static constexpr uint32_t TMEM_COLS = 512;           // two 256-column fp32 slots
+  static constexpr uint32_t TMEM_COLS = 2 * MMA_N;     // two MMA_N-column fp32 slots
   static constexpr uint32_t MMA_M = BM * CG;
   static constexpr uint32_t IDESC =
       idesc_f32acc(AB == DT_BF16 ? 1u : 0u, AB == DT_BF16 ? 1u : 0u, MMA_M, MMA_N);
   static constexpr uint32_t MAX_SMEM = 232448;         // 227 KB opt-in per CTA
-  static constexpr uint32_t BAR_BYTES = 576;
+  static constexpr uint32_t BAR_BYTES = 448;
   // CLC response ring depth: the scheduler may run this many tiles ahead of the
   // slowest consumer (at small K a tile is only a few stages long, and a
   // try_cancel round trip plus the pair forwarding must fit in the lead).
@@ -170,21 +173,23 @@ struct GemmCfg {
   static uint32_t smem_bytes(uint32_t stages) {
     return stages * STAGE + EPI_BYTES + BAR_BYTES + ALIGN_SLACK;
   }
-  static_assert(NH == 1 || (NH == 2 && CG == 2), "512-wide tiles are built for CTA pairs");
-  static_assert(SCHED != SCHED_STREAMK || NH == 1, "stream-K uses 256-wide tiles");
-  static_assert(SCHED != SCHED_SHARE || (CG == 2 && NH == 2 && ATOMS == 1),
-                "B sharing is built for 256 x 512 pair tiles (one contiguous B box per half)");
-  // stream-K partial of one CTA: 128 rows x 256 fp32 columns
+  static_assert(TN == 128 || TN == 256 || TN == 512, "tile widths 128, 256 and 512");
+  static_assert(NH == 1 || CG == 2, "512-wide tiles are built for CTA pairs");
+  static_assert(TN != 128 || CG == 2, "128-wide tiles are built for CTA pairs");
+  static_assert(SCHED != SCHED_STREAMK || NH == 1, "stream-K uses tiles of one MMA width");
+  static_assert(EPI_CHUNKS_PER_WARP >= 1, "every epilogue warp owns at least one chunk");
+  // stream-K partial of one CTA: 128 rows x MMA_N fp32 columns
   static constexpr uint32_t SK_FLOATS = BM * MMA_N;
   static_assert(MAX_STAGES <= 8, "the barrier block holds 8 ring stages");
   static_assert(CLC_SLOTS <= 8, "the barrier block holds 8 CLC response slots");
 };
 
-template <int AB, int CD, int CG, int SCHED, int NH>
+template <int AB, int CD, int CG, int SCHED, int TN>
 __global__ void __launch_bounds__(384, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const KParams p) {
-  using Cfg = GemmCfg<AB, CD, CG, SCHED, NH>;
+  using Cfg = GemmCfg<AB, CD, CG, SCHED, TN>;
+  constexpr int NH = Cfg::NH;
   extern __shared__ uint8_t smem_raw[];
 
   // ---- shared-memory carve-up (1024-byte aligned for SWIZZLE_128B) ----
@@ -200,8 +205,8 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t sBar = sEpi + Cfg::EPI_BYTES;
   uint8_t* bar_ptr = base_ptr + (sBar - base);
   // 8-byte barriers and words: full[8], empty[8], tfull[2], tempty[2], done, skdone,
-  // the TMEM base address, the abort flag; then the CLC ring (sfull, sempty, 16-byte
-  // responses) and the B-sharing barriers (own, fwd)
+  // the TMEM base address, the abort flag, the two producers' issued-stage counts
+  // (pair error drain); then the CLC ring (sfull, sempty, 16-byte responses)
   const uint32_t bar_full = sBar;
   const uint32_t bar_empty = sBar + 64;
   const uint32_t bar_tfull = sBar + 128;
@@ -210,33 +215,24 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t bar_skdone = sBar + 168;               // stream-K: partial written
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 176);
   volatile uint32_t* abort_flag = reinterpret_cast<volatile uint32_t*>(bar_ptr + 180);
+  const uint32_t abort_addr = sBar + 180;
+  // issued[r] = k-block stages the producer of in-pair rank r issued (rank 1 writes
+  // its count into the leader's word over DSMEM)
+  volatile uint32_t* issued_words = reinterpret_cast<volatile uint32_t*>(bar_ptr + 184);
+  const uint32_t issued_addr = sBar + 184;
   const uint32_t bar_sfull = sBar + 192;                // CLC_SLOTS (≤ 8)
   const uint32_t bar_sempty = sBar + 256;               // CLC_SLOTS
   const uint32_t clc_resp = sBar + 320;                 // CLC_SLOTS × 16 B
-  const uint32_t bar_own = sBar + 448;                  // SCHED_SHARE: own B box landed [8]
-  const uint32_t bar_fwd = sBar + 512;                  // SCHED_SHARE: forwarded B box in [8]
 
   const uint32_t warp = warp_id(), lane = lane_id();
-  // Cluster rank; in-pair rank (0 = the pair's MMA leader); the leader's cluster rank.
-  // SCHED_SHARE launches prefer 4-CTA clusters (two pairs, which share B) and fall
-  // back to plain pairs where 4 CTAs do not fit in a GPC.
-  const uint32_t crank = (CG == 2) ? cluster_ctarank() : 0u;
-  const uint32_t rank = crank & 1u;
-  const uint32_t lead = crank & ~1u;
-  bool share = false;
-  if constexpr (SCHED == SCHED_SHARE) share = cluster_nctarank() == 4u;
-  const uint32_t pair_mask = 3u << lead;              // commit mask: this pair
-  const uint32_t empty_mask = share ? 0xFu : pair_mask; // stage release: both pairs
-  const uint32_t xpeer = crank ^ 2u;                  // same in-pair rank, other pair
+  // In-pair rank (0 = the pair's MMA leader).
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+  const uint32_t peer = rank ^ 1u;
 
   if (warp == 0 && lane == 0) {
     for (uint32_t s = 0; s < S; ++s) {
-      // sharing: the leader's arm (A bytes) + one relay arrive per CTA of the pair
-      mbar_init(bar_full + 8 * s, share ? 3 : 1);
-      // sharing: a stage is reused only once both pairs' MMAs have read it
-      mbar_init(bar_empty + 8 * s, share ? 2 : 1);
-      mbar_init(bar_own + 8 * s, 1);
-      mbar_init(bar_fwd + 8 * s, 1);
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
     }
     for (uint32_t a = 0; a < 2; ++a) {
       mbar_init(bar_tfull + 8 * a, 1);
@@ -252,6 +248,8 @@ __global__ void __launch_bounds__(384, 1)
     mbar_init(bar_done, 1);
     mbar_init(bar_skdone, Cfg::EPI_WARPS);
     *abort_flag = 0u;
+    issued_words[0] = 0u;
+    issued_words[1] = 0u;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -270,33 +268,26 @@ __global__ void __launch_bounds__(384, 1)
   griddep_wait();
   griddep_launch_dependents();
 
+  // A role that gives up raises the abort flag of its own CTA and, in a pair, of the
+  // peer too, so the other CTA's waits stop early and both CTAs agree at teardown
+  // that the pair aborted. (The peer is alive: fail() is only called before the
+  // teardown cluster barrier, or by the leader's drain while the peer waits in the
+  // second one.)
   auto fail = [&](uint32_t code) {
     *abort_flag = 1u;
+    if constexpr (CG == 2) st_shared_cluster_u32(mapa_shared(abort_addr, peer), 1u);
     if (p.status) atomicOr(p.status, code | ST_ABORTED);
   };
 
-  // ---- TMEM slots: tile `it`, N-half h -> slot; each use of a slot flips its phase ----
+  // ---- TMEM slots: tile `it`, MMA h -> slot; each use of a slot flips its phase ----
   // NH = 1: tiles alternate between the two slots (double buffering).
-  // NH = 2: every tile uses both slots, half h in slot h.
+  // NH = 2: every tile uses both slots, MMA h in slot h.
   auto acc_slot = [](uint32_t it, int h) -> uint32_t { return NH == 1 ? (it & 1u) : uint32_t(h); };
   auto acc_use = [](uint32_t it) -> uint32_t { return NH == 1 ? (it >> 1) : it; };
 
   // ---- tile id -> (block-row, block-col) ----
-  // SCHED_SHARE: tiles 2u and 2u+1 are the upper and lower halves of super-tile u (two
-  // vertically adjacent pair tiles with the same columns), super-tiles in group-M order
-  // with groups of G/2 super-rows. The static stride is even, so the two pairs of a
-  // 4-CTA cluster (pair slots 2c, 2c+1) always hold the two halves of one super-tile.
-  // A lower half past the last block-row (odd row count) is computed on zero-filled A
-  // and not stored.
   auto tile_coords = [&](uint32_t tile, uint32_t& bm, uint32_t& bn) {
-    if constexpr (SCHED == SCHED_SHARE) {
-      uint32_t sm;
-      const uint32_t g2 = p.group_m > 1u ? p.group_m / 2u : 1u;
-      tile_to_bmn(tile >> 1, (p.m_tiles + 1u) / 2u, p.n_tiles, g2, sm, bn);
-      bm = 2u * sm + (tile & 1u);
-    } else {
-      tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
-    }
+    tile_to_bmn(tile, p.m_tiles, p.n_tiles, p.group_m, bm, bn);
   };
 
   // ---- tile sequence shared by every role ----
@@ -305,10 +296,18 @@ __global__ void __launch_bounds__(384, 1)
   //               leader's try_cancel returns (forwarded to the peer)
   const uint32_t first_tile = blockIdx.x / CG;
   const uint32_t tile_stride = gridDim.x / CG;
-  const uint32_t leader_sempty0 = (CG == 2) ? mapa_shared(bar_sempty, lead) : bar_sempty;
+  const uint32_t leader_sempty0 = (CG == 2) ? mapa_shared(bar_sempty, 0) : bar_sempty;
 
   // Consumer side of the CLC ring: wait for slot, decode, release it to the leader.
   // Returns false when the grid is exhausted (tile unchanged) or on abort.
+  // The release must follow the read of the response: the scheduler rewrites the
+  // slot (try_cancel in the leader, a DSMEM store in the peer) as soon as all 10 * CG
+  // consumers have released it. A relaxed arrive alone does not order the earlier
+  // ld.shared, so a consumer whose load waited behind long-latency stores (an
+  // epilogue warp with multimem stores to other GPUs in flight) could decode the
+  // slot's NEXT response, drop out of the tile sequence and leave the pair's TMEM
+  // hand-off waiting; fence_release_smem() orders the load without waiting for the
+  // warp's global stores.
   uint32_t sched_slot = 0, sched_phase = 0;
   auto clc_next = [&](uint32_t& tile) -> bool {
     if (!mbar_wait<CG == 2>(bar_sfull + 8 * sched_slot, sched_phase, p.wait_ns, abort_flag)) {
@@ -317,8 +316,12 @@ __global__ void __launch_bounds__(384, 1)
     }
     uint32_t x = 0;
     const bool got = clc_decode(clc_resp + 16 * sched_slot, x);
-    if constexpr (CG == 1) mbar_arrive(bar_sempty + 8 * sched_slot);
-    else mbar_arrive_cluster_relaxed(leader_sempty0 + 8 * sched_slot);  // slot read: relaxed
+    if constexpr (CG == 1) {
+      mbar_arrive(bar_sempty + 8 * sched_slot);  // release.cta: orders the read
+    } else {
+      fence_release_smem();
+      mbar_arrive_cluster_relaxed(leader_sempty0 + 8 * sched_slot);
+    }
     if (++sched_slot == Cfg::CLC_SLOTS) { sched_slot = 0; sched_phase ^= 1u; }
     if (got) tile = x / CG;
     return got;
@@ -394,8 +397,9 @@ __global__ void __launch_bounds__(384, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
-      const uint64_t hint = policy_evict_normal();
-      const uint32_t leader_full0 = (CG == 2) ? mapa_shared(bar_full, lead) : bar_full;
+      const uint64_t hint_a = (p.l2_policy & 1u) ? policy_evict_last() : policy_evict_normal();
+      const uint64_t hint_b = (p.l2_policy & 2u) ? policy_evict_first() : policy_evict_normal();
+      const uint32_t leader_full0 = (CG == 2) ? mapa_shared(bar_full, 0) : bar_full;
       if (!p.fault_inject) {
         WorkItem cur;
         bool more = first_item(cur);
@@ -405,7 +409,7 @@ __global__ void __launch_bounds__(384, 1)
           uint32_t bm, bn;
           tile_coords(cur.tile, bm, bn);
           const int32_t a_row = int32_t((bm * CG + rank) * Cfg::BM);
-          // rows of this CTA's share of N-half h: bn*BN + h*256 + rank*B_HALF_ROWS
+          // rows of this CTA's share of MMA h: bn*BN + h*MMA_N + rank*B_HALF_ROWS
           const int32_t b_row = int32_t(bn * Cfg::BN + rank * Cfg::B_HALF_ROWS);
           for (uint32_t kb = cur.kb0; kb < cur.kb1; ++kb) {
             if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, p.wait_ns, abort_flag)) {
@@ -419,26 +423,12 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
               for (int at = 0; at < Cfg::ATOMS; ++at) {
                 const int32_t x = kx + at * Cfg::ATOM_K;
-                tma_load_2d(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM, &tmA, x, a_row, bar_full + 8 * stage, hint);
+                tma_load_2d(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM, &tmA, x, a_row, bar_full + 8 * stage, hint_a);
 #pragma unroll
                 for (int h = 0; h < NH; ++h)
                   tma_load_2d(sB + stage * Cfg::B_STAGE + at * Cfg::B_ATOM + h * Cfg::B_HALF, &tmB, x,
-                              b_row + h * Cfg::MMA_N, bar_full + 8 * stage, hint);
+                              b_row + h * Cfg::MMA_N, bar_full + 8 * stage, hint_b);
               }
-            } else if (share) {
-              // A as in a plain pair (both CTAs credit the leader, which arms A only).
-              // B: this CTA loads N-half `crank >> 1` of its rows into its own-box
-              // barrier; the forwarder copies it to the other pair and the other
-              // pair's copy of the second half lands on the forwarded-box barrier.
-              // The relay then tells the leader that this CTA's B is complete.
-              if (rank == 0) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * Cfg::A_STAGE);
-              mbar_arrive_expect_tx(bar_own + 8 * stage, Cfg::B_HALF);
-              mbar_arrive_expect_tx(bar_fwd + 8 * stage, Cfg::B_HALF);
-              const uint32_t lf = leader_full0 + 8 * stage;
-              const int h = int(crank >> 1);
-              tma_load_2d_pair(sA + stage * Cfg::A_STAGE, &tmA, kx, a_row, lf, hint);
-              tma_load_2d(sB + stage * Cfg::B_STAGE + h * Cfg::B_HALF, &tmB, kx, b_row + h * Cfg::MMA_N,
-                          bar_own + 8 * stage, hint);
             } else {
               // Both CTAs' bytes are credited to the leader's full barrier; only the
               // leader arms it (a peer credit that lands first leaves the tx count
@@ -448,11 +438,11 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
               for (int at = 0; at < Cfg::ATOMS; ++at) {
                 const int32_t x = kx + at * Cfg::ATOM_K;
-                tma_load_2d_pair(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM, &tmA, x, a_row, lf, hint);
+                tma_load_2d_pair(sA + stage * Cfg::A_STAGE + at * Cfg::A_ATOM, &tmA, x, a_row, lf, hint_a);
 #pragma unroll
                 for (int h = 0; h < NH; ++h)
                   tma_load_2d_pair(sB + stage * Cfg::B_STAGE + at * Cfg::B_ATOM + h * Cfg::B_HALF, &tmB, x,
-                                   b_row + h * Cfg::MMA_N, lf, hint);
+                                   b_row + h * Cfg::MMA_N, lf, hint_b);
               }
             }
             ++issued;
@@ -463,21 +453,26 @@ __global__ void __launch_bounds__(384, 1)
           more = next_more;
         }
       }
-      if (!ok || *abort_flag) {
-        // Error path: wait (bounded) for the loads this CTA still has in flight so
-        // that no TMA write lands after the CTA's shared memory is released.
-        if constexpr (CG == 1) {
+      if constexpr (CG == 1) {
+        if (!ok || *abort_flag) {
+          // Error path: wait (bounded) for the loads this CTA still has in flight so
+          // that no TMA write lands after the CTA's shared memory is released. Every
+          // stage before the last S was consumed by the MMA, so only the last S can
+          // still be in flight.
           const uint32_t first = issued > S ? issued - S : 0u;
           for (uint32_t i = first; i < issued; ++i) {
-            if (!mbar_wait_bounded(bar_full + 8 * (i % S), (i / S) & 1u, p.wait_ns)) break;
-          }
-        } else {
-          // The pair's full barriers live in the leader; give in-flight copies a
-          // fixed 50 us (a 32 KB TMA completes in a few us) before the cluster exits.
-          const uint64_t t0 = globaltimer_ns();
-          while (globaltimer_ns() - t0 < 50000ull) {
+            if (!mbar_wait_bounded(bar_full + 8 * (i % S), (i / S) & 1u, p.wait_ns)) {
+              fail(ST_DRAIN);
+              break;
+            }
           }
         }
+      } else {
+        // The pair's loads are credited to the leader's full barriers, so the leader
+        // drains both CTAs' copies after the roles have stopped (teardown below). It
+        // needs both counts; the store is ordered before the teardown cluster barrier.
+        if (rank == 0) issued_words[0] = issued;
+        else st_shared_cluster_u32(mapa_shared(issued_addr + 4, 0), issued);
       }
     }
     __syncwarp();
@@ -524,16 +519,16 @@ __global__ void __launch_bounds__(384, 1)
             }
             if (kb + 1 == cur.kb1) {
               // Slot h is final once these MMAs complete: signal it now, so with two
-              // halves the epilogue drains slot 0 while the last half-1 MMAs run.
+              // MMAs per tile the epilogue drains slot 0 while the last MMAs into
+              // slot 1 run.
               if constexpr (CG == 1) umma_commit<1>(bar_tfull + 8 * slot);
-              else umma_commit_pair(bar_tfull + 8 * slot, uint16_t(pair_mask));
+              else umma_commit_pair(bar_tfull + 8 * slot, uint16_t(3u));
             }
           }
           if (!ok) break;
-          // frees this stage in both CTAs once the MMAs above have read it (sharing:
-          // in all four CTAs, whose empty barriers wait for both pairs' commits)
+          // frees this stage in both CTAs once the MMAs above have read it
           if constexpr (CG == 1) umma_commit<1>(bar_empty + 8 * stage);
-          else umma_commit_pair(bar_empty + 8 * stage, uint16_t(empty_mask));
+          else umma_commit_pair(bar_empty + 8 * stage, uint16_t(3u));
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
@@ -559,13 +554,17 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t peer_sfull0 = (CG == 2) ? mapa_shared(bar_sfull, 1) : 0u;
         const uint32_t peer_resp0 = (CG == 2) ? mapa_shared(clc_resp, 1) : 0u;
         while (true) {
-          if (!mbar_wait(bar_sempty + 8 * slot, ph ^ 1u, p.wait_ns, abort_flag)) {
+          // every consumer of both CTAs has read the slot's previous response
+          // (acquire.cluster pairs with the peers' fence_release_smem + arrive)
+          if (!mbar_wait<CG == 2>(bar_sempty + 8 * slot, ph ^ 1u, p.wait_ns, abort_flag)) {
             fail(ST_SCHED);
             break;
           }
           mbar_arrive_expect_tx(bar_sfull + 8 * slot, 16);
           clc_try_cancel(clc_resp + 16 * slot, bar_sfull + 8 * slot);
-          if (!mbar_wait(bar_sfull + 8 * slot, ph, p.wait_ns, abort_flag)) {
+          // The response is an async write into this CTA's shared memory: wait for it
+          // even when the CTA is aborting, so that it cannot land after the CTA exits.
+          if (!mbar_wait_bounded(bar_sfull + 8 * slot, ph, p.wait_ns)) {
             fail(ST_SCHED);
             break;
           }
@@ -582,72 +581,6 @@ __global__ void __launch_bounds__(384, 1)
           if (++slot == Cfg::CLC_SLOTS) { slot = 0; ph ^= 1u; }
         }
       }
-    } else if constexpr (SCHED == SCHED_SHARE) {
-      // ================================ B relay ================================
-      // Once this CTA holds both B boxes of a stage (its own load and the other
-      // pair's copy), tell the pair leader, whose full barrier counts one relay
-      // arrive per CTA of the pair on top of the A bytes.
-      if (lane == 0 && share) {
-        const uint32_t leader_full0 = mapa_shared(bar_full, lead);
-        uint32_t stage = 0, phase = 0;
-        bool ok = true;
-        WorkItem cur;
-        bool more = first_item(cur);
-        while (more && ok) {
-          WorkItem nxt;
-          const bool next_more = next_item(cur, nxt);
-          for (uint32_t kb = cur.kb0; kb < cur.kb1; ++kb) {
-            if (!mbar_wait(bar_own + 8 * stage, phase, p.wait_ns, abort_flag) ||
-                !mbar_wait<true>(bar_fwd + 8 * stage, phase, p.wait_ns, abort_flag)) {
-              fail(ST_SHARE);
-              ok = false;
-              break;
-            }
-            mbar_arrive_cluster(leader_full0 + 8 * stage);
-            if (++stage == S) { stage = 0; phase ^= 1u; }
-          }
-          cur = nxt;
-          more = next_more;
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == 3) {
-    // ============================== B forwarder ==============================
-    // SCHED_SHARE in a 4-CTA cluster: copy this CTA's own B box of every stage into
-    // the same place of the other pair's CTA with the same in-pair rank. That CTA's
-    // stage is free: this CTA's own load was issued only after its empty barrier saw
-    // both pairs' MMAs release the stage.
-    if constexpr (SCHED == SCHED_SHARE) {
-      if (lane == 0 && share) {
-        const uint32_t h = crank >> 1;
-        uint32_t stage = 0, phase = 0;
-        bool ok = true;
-        WorkItem cur;
-        bool more = first_item(cur);
-        while (more && ok) {
-          WorkItem nxt;
-          const bool next_more = next_item(cur, nxt);
-          for (uint32_t kb = cur.kb0; kb < cur.kb1; ++kb) {
-            if (!mbar_wait(bar_own + 8 * stage, phase, p.wait_ns, abort_flag)) {
-              fail(ST_SHARE);
-              ok = false;
-              break;
-            }
-            const uint32_t box = sB + stage * Cfg::B_STAGE + h * Cfg::B_HALF;
-            bulk_copy_s2c(mapa_shared(box, xpeer), box, Cfg::B_HALF, mapa_shared(bar_fwd + 8 * stage, xpeer));
-            if (++stage == S) { stage = 0; phase ^= 1u; }
-          }
-          cur = nxt;
-          more = next_more;
-        }
-        if (!ok || *abort_flag) {
-          // give copies still reading this CTA's shared memory a fixed 50 us
-          const uint64_t t0 = globaltimer_ns();
-          while (globaltimer_ns() - t0 < 50000ull) {
-          }
-        }
-      }
     }
     __syncwarp();
   } else if (warp >= 4) {
@@ -658,7 +591,9 @@ __global__ void __launch_bounds__(384, 1)
     if (p.scale_a) scale *= __ldg(p.scale_a);
     if (p.scale_b) scale *= __ldg(p.scale_b);
     const uint32_t my_buf = sEpi + (warp - 4) * Cfg::EPI_BUF;
-    const uint32_t leader_tempty0 = (CG == 2) ? mapa_shared(bar_tempty, lead) : bar_tempty;
+    const bool c_hint = (p.l2_policy & 4u) != 0u;
+    const uint64_t hint_c = policy_evict_first();
+    const uint32_t leader_tempty0 = (CG == 2) ? mapa_shared(bar_tempty, 0) : bar_tempty;
     uint32_t tile_iter = 0;
     WorkItem cur;
     bool more = first_item(cur);
@@ -728,16 +663,18 @@ __global__ void __launch_bounds__(384, 1)
           else mbar_arrive_cluster_relaxed(leader_tempty0 + 8 * slot);  // TMEM read: relaxed
         }
         if constexpr (SCHED == SCHED_STREAMK) {
-          // Each thread owns 128 consecutive fp32 values (its row, its columns of the
-          // slot); the workspace stores them thread-major so that every access of a
-          // warp is 512 contiguous bytes: float4 j of warp w4, lane l at (w4*32+j)*32+l.
+          // Each thread owns EPI_VALS consecutive fp32 values (its row, its columns of
+          // the slot); the workspace stores them thread-major so that every access of
+          // a warp is 512 contiguous bytes: float4 j of warp w4, lane l at
+          // (w4*J + j)*32 + l, J = EPI_VALS / 4.
+          constexpr uint32_t J = Cfg::EPI_VALS / 4;
           const uint32_t w4 = warp - 4;
           if (cur.kind == ITEM_PARTIAL) {
             float4* ws = reinterpret_cast<float4*>(p.sk_work) + size_t(worker * CG + rank) * (Cfg::SK_FLOATS / 4);
 #pragma unroll
-            for (uint32_t j = 0; j < 32; ++j) {
+            for (uint32_t j = 0; j < J; ++j) {
               const uint32_t f = 4 * j, cc = f / Cfg::EPI_COLS, x = f % Cfg::EPI_COLS;
-              __stcg(ws + (w4 * 32 + j) * 32 + lane,
+              __stcg(ws + (w4 * J + j) * 32 + lane,
                      make_float4(__uint_as_float(r[cc][x]), __uint_as_float(r[cc][x + 1]),
                                  __uint_as_float(r[cc][x + 2]), __uint_as_float(r[cc][x + 3])));
             }
@@ -776,9 +713,9 @@ __global__ void __launch_bounds__(384, 1)
               const float4* src =
                   reinterpret_cast<const float4*>(p.sk_work) + size_t(w2 * CG + rank) * (Cfg::SK_FLOATS / 4);
 #pragma unroll
-              for (uint32_t j = 0; j < 32; ++j) {
+              for (uint32_t j = 0; j < J; ++j) {
                 const uint32_t f = 4 * j, cc = f / Cfg::EPI_COLS, x = f % Cfg::EPI_COLS;
-                const float4 v = __ldcg(src + (w4 * 32 + j) * 32 + lane);
+                const float4 v = __ldcg(src + (w4 * J + j) * 32 + lane);
                 r[cc][x] = __float_as_uint(__uint_as_float(r[cc][x]) + v.x);
                 r[cc][x + 1] = __float_as_uint(__uint_as_float(r[cc][x + 1]) + v.y);
                 r[cc][x + 2] = __float_as_uint(__uint_as_float(r[cc][x + 2]) + v.z);
@@ -816,7 +753,10 @@ __global__ void __launch_bounds__(384, 1)
           __syncwarp();
           const uint32_t col0 = bn * Cfg::BN + h * Cfg::MMA_N + (c0 + cc) * Cfg::EPI_COLS;
           if (lane == 0) {
-            if (uint32_t(row0) < p.M && col0 < p.N) tma_store_2d(&tmC, sb, int32_t(col0), row0);
+            if (uint32_t(row0) < p.M && col0 < p.N) {
+              if (c_hint) tma_store_2d_hint(&tmC, sb, int32_t(col0), row0, hint_c);
+              else tma_store_2d(&tmC, sb, int32_t(col0), row0);
+            }
             bulk_commit();
           }
           if (p.gather_mode != GATHER_OFF) {
@@ -859,7 +799,38 @@ __global__ void __launch_bounds__(384, 1)
 
   // ---- teardown: every role has left its loop; release TMEM ----
   tc_fence_before();
-  if constexpr (CG == 2) cluster_sync(); else __syncthreads();
+  if constexpr (CG == 2) {
+    cluster_sync();
+    // Error drain of the pair. Both CTAs' TMA loads are credited to the leader's full
+    // barriers, so a CTA cannot see its own loads land. After an abort in either CTA,
+    // the leader's producer thread waits for every stage still in flight, completing
+    // the phases whose bytes will never come, before either CTA leaves: at most the
+    // last S stages of either producer can be unconsumed (a producer issues stage i
+    // only after the MMA consumed stage i - S, which needed both producers' bytes).
+    // fail() raises both CTAs' flags before the barrier above, so both CTAs agree on
+    // the extra barrier below.
+    if (*abort_flag) {
+      if (warp == 0 && lane == 0 && rank == 0) {
+        const uint32_t il = issued_words[0], ip = issued_words[1];
+        const uint32_t hi = il > ip ? il : ip;
+        for (uint32_t i = hi > S ? hi - S : 0u; i < hi; ++i) {
+          const uint32_t bar = bar_full + 8 * (i % S);
+          // A phase with a missing half cannot have completed, so the fix-ups below
+          // only touch phases still open: the leader never armed stage i (wait for
+          // the peer's bytes alone), or the peer never loaded it (take its bytes off).
+          if (i >= il) mbar_arrive_expect_tx(bar, Cfg::STAGE);
+          else if (i >= ip) mbar_complete_tx(bar, Cfg::STAGE);
+          if (!mbar_wait_bounded(bar, (i / S) & 1u, p.wait_ns)) {
+            fail(ST_DRAIN);
+            break;
+          }
+        }
+      }
+      cluster_sync();
+    }
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<CG>(tmem_base, Cfg::TMEM_COLS);

@@ -31,6 +31,7 @@
 // stream capture starts. Later calls only read the cached address.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 
@@ -44,15 +45,18 @@ constexpr size_t kScratchBytes = 256;
 static __device__ __align__(256) uint32_t g_noalloc_scratch[kScratchBytes / sizeof(uint32_t)];
 
 std::mutex g_mu;
-uint32_t* g_scratch_dev[64] = {nullptr};  // device address of g_noalloc_scratch, per device
+// Device address of g_noalloc_scratch, per device. Published with a release store
+// after g_sms and g_cc_major are written and read with an acquire load, so a thread
+// that finds the address also finds the SM count it needs to pick a variant.
+std::atomic<uint32_t*> g_scratch_dev[64];
 int g_sms[64] = {0};
 int g_cc_major[64] = {0};
 
 // Once per device, with `dev` current: everything the launch needs, no allocation.
 int setup_device(int dev) {
-  if (g_scratch_dev[dev]) return B200_OK;
+  if (g_scratch_dev[dev].load(std::memory_order_acquire)) return B200_OK;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_scratch_dev[dev]) return B200_OK;
+  if (g_scratch_dev[dev].load(std::memory_order_relaxed)) return B200_OK;
   int rc = b200::gemm_resolve_driver();
   if (rc != B200_OK) return rc;
   int sms = 0, major = 0;
@@ -65,7 +69,7 @@ int setup_device(int dev) {
     return B200_ERR_CUDA;
   g_sms[dev] = sms;
   g_cc_major[dev] = major;
-  g_scratch_dev[dev] = static_cast<uint32_t*>(ptr);
+  g_scratch_dev[dev].store(static_cast<uint32_t*>(ptr), std::memory_order_release);
   return B200_OK;
 }
 
@@ -90,7 +94,7 @@ extern "C" int b200_gemm_noalloc(const B200GemmArgs* args, void* stream_v, int c
   rc = setup_device(dev);
   if (rc != B200_OK) return rc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
-  uint32_t* status = g_scratch_dev[dev];
+  uint32_t* status = g_scratch_dev[dev].load(std::memory_order_acquire);
   // The array keeps the previous call's value: start this call's word at zero.
   if (cudaMemsetAsync(status, 0, sizeof(uint32_t), stream) != cudaSuccess) return B200_ERR_CUDA;
   rc = b200::gemm_launch_impl(a, stream, g_sms[dev], g_cc_major[dev], status, /*allow_workspace=*/false);

@@ -76,15 +76,35 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Relaxed remote arrive, for "I have finished READING this" signals (a consumed CLC
-// response slot, a drained TMEM accumulator): the reads are complete before the
-// arrive executes (their values are in registers: the response was decoded, and
-// tcgen05.wait::ld returned), so no release ordering is needed. A release.cluster
-// arrive also waits for this thread's earlier memory operations (e.g. the epilogue's
-// in-flight TMA stores) to become visible cluster-wide, which measured ~1 us per
-// arrive and stalled the pair kernels' MMA and scheduler.
+// Relaxed remote arrive. On its own it orders nothing: the memory model lets it
+// become visible before this thread's earlier loads have read their data. Two uses:
+//   * a drained TMEM accumulator: tcgen05.wait::ld has returned, so the TMEM reads
+//     are complete, and the arrive only has to follow them (no release needed);
+//   * after fence_release_smem(): the fence orders this thread's earlier shared::cta
+//     accesses (the ld.shared of a CLC response) before the arrive.
+// A release.cluster arrive would also wait for this thread's earlier global and bulk
+// stores (an epilogue warp's TMA stores, or its multimem stores to other GPUs) to
+// become visible cluster-wide: measured ~1 us per arrive, which stalled the pair
+// kernels' MMA and scheduler.
 __device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+// Release fence restricted to shared::cta: this thread's earlier shared::cta loads
+// and stores are ordered before its following (relaxed) mbarrier arrive on a
+// shared::cluster barrier, without waiting for its global or bulk stores. Paired
+// with an acquire.cluster wait on that barrier, it makes "I have read this slot"
+// safe to act on: the slot's next writer cannot overtake the read.
+__device__ __forceinline__ void fence_release_smem() {
+  asm volatile("fence.release.sync_restrict::shared::cta.cluster;" ::: "memory");
+}
+
+// Take `bytes` off the pending transaction count of the current phase, as if that
+// many bytes of an async copy had landed. Used only on the error path, to complete
+// a phase whose expected bytes will never come.
+__device__ __forceinline__ void mbar_complete_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
 }
 
@@ -205,6 +225,16 @@ __device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, uint
                : "memory");
 }
 
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_shared_cluster_u32(uint32_t cluster_addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void ld_shared_v4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c,
                                              uint32_t& d) {
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(addr)
@@ -245,16 +275,12 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, uint32_t src,
                : "memory");
 }
 
-// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this
-// CTA's shared memory into another CTA's shared memory of the cluster; completion is
-// counted on `mbar_cluster`, a barrier in the destination CTA. A plain point-to-point
-// copy between SMs: no global memory is read and nothing is multicast.
-__device__ __forceinline__ void bulk_copy_s2c(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
-                                              uint32_t mbar_cluster) {
+// Same, with an L2 cache policy for the written lines.
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* m, uint32_t src, int32_t x, int32_t y,
+                                                  uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst_cluster),
-      "r"(src), "r"(bytes), "r"(mbar_cluster)
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%1, %2}], [%3], %4;" ::"l"(m),
+      "r"(x), "r"(y), "r"(src), "l"(policy)
       : "memory");
 }
 
@@ -297,6 +323,11 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
 __device__ __forceinline__ uint64_t policy_evict_normal() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 

@@ -142,6 +142,7 @@ inline const char* variant_name(int v) {
     case B200_VARIANT_PERSISTENT: return "persistent";
     case B200_VARIANT_CLC: return "clc";
     case B200_VARIANT_2CTA_CLC: return "2cta_clc";
+    case B200_VARIANT_2CTA_STREAMK: return "2cta_streamk";
     default: return "auto";
   }
 }

@@ -20,8 +20,11 @@
  *   - Stream-ordered and asynchronous; thread-safe; no allocation on the hot path
  *     (the per-device status word is allocated once, on the first call on a device;
  *     the stream-K workspace, 32 MB, once on the first stream-K call on a device).
- *   - Stream-K launches on one device share that workspace: launches that overlap
- *     on the GPU (different streams) must not both use stream-K.
+ *   - Stream-K launches on one device share that workspace, so the library orders
+ *     them: a stream-K launch on a stream other than the previous stream-K launch's
+ *     first waits (cudaStreamWaitEvent) for that launch to finish. Inside a stream
+ *     capture nothing is recorded or waited for; the captured graph must order its
+ *     stream-K launches itself (one stream, or explicit dependencies).
  *   - Device-side waits are bounded: a protocol failure sets the device status
  *     word, which b200_gemm_status() reads back as B200_ERR_DEVICE_TIMEOUT.
  */
@@ -34,7 +37,7 @@
 extern "C" {
 #endif
 
-#define B200GEMM_ABI_VERSION 3
+#define B200GEMM_ABI_VERSION 4
 
 /* element types */
 enum {
@@ -59,15 +62,9 @@ enum {
   B200_VARIANT_2CTA_STREAMK = 6 /* cta_group::2 pair, stream-K: every pair takes an equal
                                   share of the tile x k-block iterations; split tiles are
                                   summed in a fixed order through a library-owned fp32
-                                  workspace; AUTO takes it only when the tiles would
-                                  leave three quarters of the pairs idle and K is long */,
-  B200_VARIANT_2CTA_SHARE = 7  /* two cta_group::2 pairs per 4-CTA cluster (2-CTA where a
-                                  GPC has no room for 4) computing vertically adjacent
-                                  256x512 tiles; each CTA loads half of its B rows and
-                                  copies them to the other pair over DSMEM (no
-                                  multicast load): a third less L2 traffic per flop,
-                                  but slower than 2CTA on B200 (SM-to-SM copies stream
-                                  at ~32 GB/s per SM); never picked by AUTO          */
+                                  workspace; AUTO takes it only when 256-wide tiles
+                                  would leave three quarters of the pairs idle and K is
+                                  at least 6144                                          */
 };
 
 /* return codes */
@@ -101,8 +98,11 @@ typedef struct B200GemmArgs {
   int32_t fault_inject;    /* 0 in production; 1 = test hook: producer issues no loads,
                               so the bounded waits must report a device timeout          */
   uint64_t wait_limit_ns;  /* bound of each device wait, 0 = library default (1 s)       */
-  int32_t tile_n;          /* C columns per tile: 0 = library default, 256, or 512 (the
-                              512-wide tile exists for the pair variants only)          */
+  int32_t tile_n;          /* C columns per tile: 0 = library default, 128, 256 or 512.
+                              1-CTA variants: 256 only; pair variants: 128, 256, 512
+                              (stream-K: 128 or 256). The default picks by wave count:
+                              512 for long-K multi-wave problems, 128 where 256-wide
+                              tiles would leave pairs idle, else 256                    */
   int32_t reserved;        /* must be 0                                                  */
 } B200GemmArgs;
 
@@ -125,6 +125,13 @@ int b200_gemm_variant_info(int32_t variant, int32_t ab_dtype, int32_t* tile_m, i
 
 /* The variant B200_VARIANT_AUTO resolves to for this problem on the current device. */
 int b200_gemm_pick_variant(const B200GemmArgs* args);
+
+/* The variant and tile width b200_gemm would launch for `args` on the current device
+ * (AUTO and tile_n = 0 resolved; explicit choices returned as given). Returns B200_OK
+ * or the code b200_gemm's argument checks would return. The reference fixes both per
+ * experiment at compile time (src/08_persistent/gemm_fp8_bn128.cu:73 is its BN=128
+ * kernel); this call exposes the library's choice to hosts, benches and tests. */
+int b200_gemm_pick_config(const B200GemmArgs* args, int32_t* variant, int32_t* tile_n);
 
 /* Allocation-free form of b200_gemm, for callers that cannot have a library call
  * cudaMalloc: code inside frameworks whose pool allocator must own every device
@@ -170,9 +177,10 @@ void b200_gemm_plan_destroy(B200GemmPlan* plan);
  * and col_off * elem multiples of 16); ldg >= col_off + N; dst 16-byte aligned (and
  * every base in the array). On return the launch is queued; G is complete on a GPU
  * once every GPU's launch has completed, so the caller synchronises the GPUs (e.g. a
- * barrier on the symmetric-memory signal pads) before reading G. Static schedules
- * only: AUTO resolves to 1CTA / PERSISTENT / 2CTA; other variants return
- * B200_ERR_UNSUPPORTED. The reference has no
+ * barrier on the symmetric-memory signal pads) before reading G. Every schedule but
+ * stream-K (whose workspace this entry point does not take; it returns
+ * B200_ERR_UNSUPPORTED); AUTO resolves as b200_gemm's does without stream-K. The
+ * reference has no
  * multi-GPU code; its planned counterpart is a separate ncclAllGather after the GEMM. */
 enum { B200_GATHER_MULTICAST = 1, B200_GATHER_PEERS = 2 };
 int b200_gemm_allgather(const B200GemmArgs* args, const void* dst, int32_t mode, int32_t npeers,

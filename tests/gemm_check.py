@@ -78,6 +78,35 @@ def reference(oracle, inp, rows=None):
     return r
 
 
+def reference_cols(oracle, inp, cols):
+    """Oracle C restricted to the columns [c0, c1): all M rows of that column slab."""
+    c0, c1 = cols
+    r = oracle.gemm_tn(inp["a_val"], inp["b_val"][c0:c1])
+    if inp["scaled"]:
+        s = np.float32(inp["sa"]) * np.float32(inp["sb"])
+        r = (r * s).astype(np.float32)
+    return r
+
+
+def check_big(oracle, inp, got, tol, seed, rows=256, band=32, slab=256):
+    """Big-shape parity: `rows` seeded rows (bands of `band` rows, the first and last
+    band included) against all N columns, plus every row of one seeded `slab`-column
+    slab of C. Returns a list of failures (empty when everything matches)."""
+    M, N = inp["M"], inp["N"]
+    fails = []
+    for r0, r1 in sample_bands(M, seed, bands=max(1, rows // band - 2), rows=band):
+        ok, info = compare(got[r0:r1], reference(oracle, inp, rows=(r0, r1)), tol)
+        if not ok:
+            fails.append(("rows", r0, r1, info))
+    rng = np.random.default_rng(seed + 1)
+    c0 = int(rng.integers(0, max(1, (N - slab) // 16 + 1))) * 16 if N > slab else 0
+    c1 = min(N, c0 + slab)
+    ok, info = compare(got[:, c0:c1], reference_cols(oracle, inp, (c0, c1)), tol)
+    if not ok:
+        fails.append(("cols", c0, c1, info))
+    return fails
+
+
 def sample_bands(M, seed, bands=4, rows=64):
     """Seeded row bands [r0, r0+rows) spread over M, for big-shape checks."""
     rng = np.random.default_rng(seed)

@@ -68,7 +68,7 @@ int main(void) {{
 
 def test_abi_version_and_strerror(b200):
     L = b200.lib()
-    assert L.b200_gemm_abi_version() == 3
+    assert L.b200_gemm_abi_version() == 4
     for code in (0, -1, -2, -3, -4, -5, -6, -7, -8, -9):
         assert b200.strerror(code)
     assert "unknown" in b200.strerror(-99)
@@ -85,16 +85,20 @@ def test_variant_info(b200):
     for v in ("2cta", "2cta_clc"):
         info = b200.variant_info(v, b200.DT_BF16, tile_n=512)
         assert info["tile_m"] == 256 and info["tile_n"] == 512 and info["max_stages"] == 4
+    for v in ("2cta", "2cta_clc", "2cta_streamk"):
+        # 256x128 pair tiles: two K atoms per stage, 48 KB, four stages
+        info = b200.variant_info(v, b200.DT_E4M3, tile_n=128)
+        assert info["tile_m"] == 256 and info["tile_n"] == 128 and info["max_stages"] == 4
     info = b200.variant_info("2cta_streamk", b200.DT_F16)
     assert info["tile_m"] == 256 and info["tile_n"] == 256 and info["max_stages"] == 3
     with pytest.raises(b200.B200Error):
-        b200.variant_info("2cta_streamk", tile_n=512)  # stream-K uses 256-wide tiles
-    info = b200.variant_info("2cta_share", b200.DT_F16)
-    assert info["tile_m"] == 256 and info["tile_n"] == 512 and info["max_stages"] == 4
+        b200.variant_info("2cta_streamk", tile_n=512)  # stream-K uses one MMA width
     with pytest.raises(b200.B200Error):
-        b200.variant_info("2cta_share", tile_n=256)  # B sharing uses 256x512 tiles
-    with pytest.raises(b200.B200Error):
-        b200.variant_info("persistent", tile_n=512)  # 512-wide tiles are pair-only
+        b200.variant_info(7)  # the former B-sharing variant is gone
+    for v in ("persistent", "1cta", "clc"):
+        for tn in (128, 512):
+            with pytest.raises(b200.B200Error):
+                b200.variant_info(v, tile_n=tn)  # narrow and wide tiles are pair-only
     with pytest.raises(b200.B200Error):
         b200.variant_info("2cta", tile_n=384)
     with pytest.raises(b200.B200Error):
@@ -119,6 +123,7 @@ def _args(b200, **kw):
     ({"ab_dtype": 3}, -1),            # f32 inputs are not a GEMM input type
     ({"c_dtype": 2}, -1),             # e4m3 output not supported
     ({"variant": 9}, -1),
+    ({"variant": 7}, -1),             # no variant 7 since ABI 4
     ({"M": -1}, -2),
     ({"K": -5}, -2),
     ({"N": 1 << 31}, -2),
@@ -171,9 +176,7 @@ def test_python_wrapper_checks_shapes(b200):
 def test_product_path_has_no_oracle_or_fallback():
     """The library and its Python mirror never reach into oracle/ or a CPU GEMM."""
     pkg = ROOT / "hopper-lab_b200"
-    product = [f for f in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cuh"))
-               # the profiling and power drivers time cuBLAS on purpose, as the reference column
-               if f.name not in ("profile_case.py", "power_case.py")]
+    product = list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cuh"))
     for f in product:
         text = f.read_text()
         assert "import oracle" not in text and "oracle/" not in text.replace("oracle/_ref", ""), f
