@@ -39,7 +39,7 @@ src/05_gemm/gemm_ws.cu:258-265, verbatim loop order, all host threads) timed on
 row bands of the same 8192^3 fp16 problem; rank 0 only.
 
 Measurement helpers (single GPU; the committed profiles/ summaries cite them):
-  --mode profile  <f16|e4m3> <ours|cublas> [variant] [size] [tile_n]: three warm-up
+  --mode profile  <f16|e4m3> <ours|cublas> [variant] [size] [tile_n] [group_m]: three warm-up
                   launches, then one inside cudaProfilerStart/Stop for
                   `ncu --profile-from-start off`.
   --mode power    <f16|bf16|e4m3> <config>...: sustained TFLOPS, energy per GEMM (NVML
@@ -698,12 +698,13 @@ def mode_profile(opt):
     variant = p[2] if len(p) > 2 else "auto"
     M_, N_, K_ = _parse_size(p[3] if len(p) > 3 else "8192")
     tile_n = int(p[4]) if len(p) > 4 else 0
+    group_m = int(p[5]) if len(p) > 5 else 0
     torch.cuda.set_device(0)
     a, b, c, sa, sb, cublas = _inputs(torch, b200, dt, M_, N_, K_)
 
     def run():
         if who == "ours":
-            b200.gemm(a, b, c, scale_a=sa, scale_b=sb, variant=variant, tile_n=tile_n)
+            b200.gemm(a, b, c, scale_a=sa, scale_b=sb, variant=variant, tile_n=tile_n, group_m=group_m)
         else:
             cublas()
 
