@@ -8,7 +8,7 @@ Objects go to ``hopper-lab_b200/_build/``; the shared library to
 
 Executables (one per reference experiment) go to ``hopper-lab_b200/bin/``.
 
-Usage: python hopper-lab_b200/build.py [--force] [-j N]
+Usage: python hopper-lab_b200/build.py [--force] [-j N] [--out DIR]
 """
 from __future__ import annotations
 
@@ -62,20 +62,24 @@ def _headers() -> list[Path]:
     return [CSRC / h for h in HEADERS] + [ROOT / "include" / "b200gemm.h"]
 
 
-def build_library(force: bool = False, jobs: int = 8) -> Path:
-    BUILD.mkdir(exist_ok=True)
-    LIB.mkdir(exist_ok=True)
+def build_library(force: bool = False, jobs: int = 8, out: Path | None = None) -> Path:
+    """lib/libb200gemm.so, or <out>/libb200gemm.so (objects in <out>/_build) for a second
+    build with other compile-time options (nvcc reads extra ones from NVCC_APPEND_FLAGS)."""
+    build = BUILD if out is None else out / "_build"
+    lib = LIB if out is None else out
+    build.mkdir(parents=True, exist_ok=True)
+    lib.mkdir(parents=True, exist_ok=True)
     objs = []
     todo = []
     for src in LIB_SOURCES:
         s = CSRC / src
-        o = BUILD / (s.stem + ".o")
+        o = build / (s.stem + ".o")
         objs.append(o)
         if force or _stale(o, [s] + _headers()):
             todo.append([NVCC, *NVFLAGS, "-c", str(s), "-o", str(o)])
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         list(ex.map(_run, todo))
-    so = LIB / "libb200gemm.so"
+    so = lib / "libb200gemm.so"
     if force or todo or _stale(so, objs):
         _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", str(so), *map(str, objs)])
     return so
@@ -119,9 +123,14 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-j", type=int, default=8)
+    ap.add_argument("--out", type=Path, default=None,
+                    help="build only the library, into this directory (e.g. an experimental build: "
+                         "NVCC_APPEND_FLAGS=-DB200_EXPERIMENT_ENV)")
     a = ap.parse_args()
-    so = build_library(force=a.force, jobs=a.j)
+    so = build_library(force=a.force, jobs=a.j, out=a.out)
     print(so)
+    if a.out is not None:
+        return
     for b in build_experiments(force=a.force, jobs=a.j):
         print(b)
 

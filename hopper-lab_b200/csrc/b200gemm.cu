@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -80,14 +81,34 @@ int g_cc_major[64] = {0};
 constexpr uint64_t kDefaultWaitNs = 1000000000ull;  // 1 s per wait
 // L2 cache policies of the operand loads and C stores (KParams::l2_policy bits): A
 // evict_last, B evict_first, C stores evict_first. Under the 1 kW power cap the clock
-// follows the energy of each GEMM, and these hints cut it: sustained 8192^3, 3 rounds
-// interleaved with cuBLASLt (bench.py --mode power), e4m3 2665-2701 TFLOPS and
-// 403-407 mJ per GEMM against 2578-2608 and 408-421 with evict_normal everywhere
-// (cuBLASLt 2616-2626), f16 1287-1294 against 1263-1276 (cuBLASLt 1306-1325).
+// follows the energy of each GEMM, and these hints cut it. Sustained 8192^3, cuBLASLt
+// interleaved in rounds (bench.py --mode power): e4m3 2665-2701 TFLOPS and 403-407 mJ
+// per GEMM against 2578-2608 and 408-421 with evict_normal everywhere; f16 1305 TFLOPS
+// and 832 mJ against 1287 and 877 (f16 reads more DRAM bytes with these hints, 1256 vs
+// 884 MB per launch, yet spends less energy per GEMM).
 #ifndef B200_L2_POLICY
 #define B200_L2_POLICY 7u
 #endif
 constexpr uint32_t kL2Policy = B200_L2_POLICY;
+
+// Experimental builds only (compiled with -DB200_EXPERIMENT_ENV, never by default):
+// the L2 policy bits and the operand maps' L2 promotion (128 or 256 bytes) come from
+// the environment variables B200_L2_POLICY and B200_L2_PROMO at every call, so that
+// bench.py --mode power can interleave cache settings inside one process.
+uint32_t l2_policy_bits() {
+#ifdef B200_EXPERIMENT_ENV
+  if (const char* e = std::getenv("B200_L2_POLICY")) return uint32_t(std::atoi(e));
+#endif
+  return kL2Policy;
+}
+CUtensorMapL2promotion l2_promotion() {
+#ifdef B200_EXPERIMENT_ENV
+  if (const char* e = std::getenv("B200_L2_PROMO"))
+    if (std::atoi(e) == 256) return CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+#endif
+  return CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
+}
+
 constexpr int kDefaultGroupM = 8;
 // 256x512 tiles are twice as wide, so twice as many block-rows per group keep a wave's
 // A and B panels balanced: at 8192^3 under the power cap, 2-4 % less energy per GEMM
@@ -164,7 +185,7 @@ int encode_2d(CUtensorMap* m, const void* ptr, int dt, uint64_t rows, uint64_t c
   std::memset(m, 0, sizeof(*m));
   CUresult r = g_encode(m, t, 2, const_cast<void*>(ptr), gdim, gstride, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        l2_promotion(), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B200_OK : B200_ERR_TMAP;
 }
 
@@ -362,7 +383,7 @@ int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status,
   kp.scale_b = a.scale_b;
   kp.status = status;
   kp.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kDefaultWaitNs;
-  kp.l2_policy = kL2Policy;
+  kp.l2_policy = l2_policy_bits();
   if (gather) {
     kp.gather = static_cast<const uint8_t*>(gather->dst);
     kp.gather_mode = gather->mode;
