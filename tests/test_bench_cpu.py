@@ -37,3 +37,20 @@ def test_roofline_traffic_comes_from_profiles():
     assert m.profile_traffic("f16_8192") > 402653184  # above the compulsory bytes
     assert m.profile_traffic("e4m3_8192") > 268435456
     assert m.profile_traffic("nonexistent") is None
+
+
+def test_measurement_modes_parse_and_size_helper():
+    """The profile / power / sweep helpers parse their arguments (positional arguments may
+    be mixed with options) and sizes like 8192, 8192x1024 and 256x16384x8192."""
+    spec = importlib.util.spec_from_file_location("bench_mod2", ROOT / "bench.py")
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    assert m._parse_size("8192") == (8192, 8192, 8192)
+    assert m._parse_size("8192x1024") == (8192, 8192, 1024)
+    assert m._parse_size("256x16384x8192") == (256, 16384, 8192)
+    for args in (["--mode", "power", "e4m3", "--shape", "256x16384x8192", "cublas", "--help"],
+                 ["--mode", "sweep", "--dtypes", "f16", "--help"],
+                 ["--mode", "profile", "f16", "ours", "--help"]):
+        r = subprocess.run([sys.executable, str(ROOT / "bench.py"), *args], capture_output=True,
+                           text=True, timeout=120, cwd=ROOT)
+        assert r.returncode == 0 and "--mode" in r.stdout, (args, r.stderr[-500:])
