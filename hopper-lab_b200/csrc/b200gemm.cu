@@ -261,11 +261,12 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // C columns per tile for a pair variant when the caller leaves tile_n = 0. Chosen from
 // launch-time sweeps on B200 (bench.py --mode sweep; medians of 30 launches):
-//   512: the 256x512 tile cuts operand traffic by a quarter (less power, so a higher
-//        clock under the power cap) but its accumulator is single-buffered, so it only
-//        pays with a long main loop (K >= 4096) and at least one full wave of wide
-//        tiles: 4096^3 f16 1366 vs 1310 TFLOPS (256-wide), 8192^3 f16 711 vs 729 us per
-//        launch; 2048x2048x8192 (32 wide tiles) 795 vs 1234.
+//   512: the 256x512 tile cuts operand traffic by a quarter (less energy per GEMM, so a
+//        higher clock under the power cap); its accumulator is single-buffered, which
+//        the main loop hides from K = 1024 on, and it needs at least one full wave of
+//        wide tiles: 4096^3 f16 1366 vs 1310 TFLOPS (256-wide), 8192^3 f16 711 vs 729 us
+//        per launch; 8192^2 x 1024 sustained e4m3 1979 vs 1900, f16 1150 vs 1092;
+//        2048x2048x8192 (32 wide tiles) 795 vs 1234.
 //   128: the 256x128 tile moves 1.5x the operand bytes per flop into each SM, and the
 //        SMs' L2 ingress caps it at ~0.7x the per-column rate of 256-wide tiles (8192^2
 //        x 1024 f16: 865 vs 1265 TFLOPS), so it is taken only where 256-wide tiles
@@ -280,7 +281,7 @@ int pick_tile_n(const B200GemmArgs* a, int variant, int sms) {
     return 256;
   if (variant == B200_VARIANT_2CTA_STREAMK) return 128;
   const int64_t pairs = sms / 2;
-  if (a->K >= 4096 && ceil_div(a->M, 256) * ceil_div(a->N, 512) >= pairs) return 512;
+  if (a->K >= 1024 && ceil_div(a->M, 256) * ceil_div(a->N, 512) >= pairs) return 512;
   if (ceil_div(a->M, 256) * ceil_div(a->N, 256) * 2 <= pairs) return 128;
   return 256;
 }

@@ -101,8 +101,8 @@ typedef struct B200GemmArgs {
   int32_t tile_n;          /* C columns per tile: 0 = library default, 128, 256 or 512.
                               1-CTA variants: 256 only; pair variants: 128, 256, 512
                               (stream-K: 128 or 256). The default picks by wave count:
-                              512 for long-K multi-wave problems, 128 where 256-wide
-                              tiles would leave pairs idle, else 256                    */
+                              512 for K >= 1024 with a full wave of wide tiles, 128
+                              where 256-wide tiles would leave pairs idle, else 256     */
   int32_t reserved;        /* must be 0                                                  */
 } B200GemmArgs;
 

@@ -386,8 +386,8 @@ def _pick(b200, M, N, K, dtype=None):
 def test_auto_choice(b200):
     """AUTO: pairs whenever they need no more waves than 1-CTA tiles (static for one
     wave, CLC work stealing for more); 256x128 pair tiles where 256-wide ones would
-    leave more than half of the pairs idle; 256x512 for long-K problems with a full wave
-    of wide tiles; stream-K (128 wide) when 256-wide tiles leave three quarters of the
+    leave more than half of the pairs idle; 256x512 for K >= 1024 with a full wave of
+    wide tiles; stream-K (128 wide) when 256-wide tiles leave three quarters of the
     pairs idle and K >= 6144; 1-CTA tiles otherwise."""
     assert _pick(b200, 512, 1024, 8192) == ("2cta_streamk", 128)
     assert _pick(b200, 1024, 1024, 8192) == ("2cta_streamk", 128)
@@ -399,7 +399,8 @@ def test_auto_choice(b200):
     assert _pick(b200, 8192, 8192, 8192) == ("2cta_clc", 512)
     assert _pick(b200, 8192, 8192, 8192, b200.DT_E4M3) == ("2cta_clc", 512)
     assert _pick(b200, 4096, 4096, 4096) == ("2cta_clc", 512)  # 128 wide tiles >= 74 pairs
-    assert _pick(b200, 8192, 8192, 1024) == ("2cta_clc", 256)  # short K: double-buffered
+    assert _pick(b200, 8192, 8192, 1024) == ("2cta_clc", 512)  # K >= 1024 hides the single slot
+    assert _pick(b200, 8192, 8192, 512) == ("2cta_clc", 256)   # shorter K: double-buffered 256
     # M = 384 rounds up to two pair rows but three 1-CTA rows: 1-CTA needs fewer waves
     assert _pick(b200, 384, 65536, 1024) == ("persistent", 256)
     assert _pick(b200, 128, 1024, 1024) == ("1cta", 256)
