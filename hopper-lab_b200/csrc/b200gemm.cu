@@ -267,23 +267,34 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 //        wide tiles: 4096^3 f16 1366 vs 1310 TFLOPS (256-wide), 8192^3 f16 711 vs 729 us
 //        per launch; 8192^2 x 1024 sustained e4m3 1979 vs 1900, f16 1150 vs 1092;
 //        2048x2048x8192 (32 wide tiles) 795 vs 1234.
-//   128: the 256x128 tile moves 1.5x the operand bytes per flop into each SM, and the
-//        SMs' L2 ingress caps it at ~0.7x the per-column rate of 256-wide tiles (8192^2
-//        x 1024 f16: 865 vs 1265 TFLOPS), so it is taken only where 256-wide tiles
-//        would leave more than half of the pairs idle: 2048x1024x4096 f16 593 vs 555,
-//        e4m3 915 vs 823; 2048x1024x8192 f16 756 vs 696. This is the reference's open
+//   128: the 256x128 tile moves 1.5x the operand bytes per flop out of L2, which caps
+//        its per-pair rate (4096x1024x8192 f16: 883 vs 1279 TFLOPS for 256-wide, e4m3
+//        1745 vs 2205), so it is taken only where 256-wide tiles would leave more than
+//        half of the pairs idle: 2048x1024x4096 f16 686 vs 589, e4m3 911 vs 819;
+//        2048x1024x8192 f16 870 vs 719, e4m3 1370 vs 1174. This is the reference's open
 //        BN=64/128 choice (docs/notes/08_persistent.md:213) decided by wave count.
 //   stream-K: 128 (its splits then cover twice the pairs per tile column): 1024x1024x
-//        16384 f16 723 vs 666 TFLOPS (256-wide), 512x1024x8192 f16 319 vs 181.
+//        16384 f16 722 vs 690 TFLOPS (256-wide), e4m3 1177 vs 872; 512x1024x8192 f16
+//        317 vs 180.
+//   An explicit ring depth (`stages`) moves the choice to the next wider tile whose ring
+//   holds it: the 256x128 pair stage is the largest (four atoms, two stages).
 int pick_tile_n(const B200GemmArgs* a, int variant, int sms) {
   if (variant != B200_VARIANT_2CTA && variant != B200_VARIANT_2CTA_CLC &&
       variant != B200_VARIANT_2CTA_STREAMK)
     return 256;
-  if (variant == B200_VARIANT_2CTA_STREAMK) return 128;
   const int64_t pairs = sms / 2;
-  if (a->K >= 1024 && ceil_div(a->M, 256) * ceil_div(a->N, 512) >= pairs) return 512;
-  if (ceil_div(a->M, 256) * ceil_div(a->N, 256) * 2 <= pairs) return 128;
-  return 256;
+  int tn = 256;
+  if (variant == B200_VARIANT_2CTA_STREAMK) tn = 128;
+  else if (a->K >= 1024 && ceil_div(a->M, 256) * ceil_div(a->N, 512) >= pairs) tn = 512;
+  else if (ceil_div(a->M, 256) * ceil_div(a->N, 256) * 2 <= pairs) tn = 128;
+  if (a->stages > 0) {
+    const int widest = (variant == B200_VARIANT_2CTA_STREAMK) ? 256 : 512;
+    for (; tn < widest; tn *= 2) {
+      VariantShape vs;
+      if (variant_shape(variant, tn, &vs) == B200_OK && uint32_t(a->stages) <= vs.max_stages) break;
+    }
+  }
+  return tn;
 }
 
 int pick_variant(const B200GemmArgs* a, int sms, bool allow_workspace) {
@@ -300,7 +311,7 @@ int pick_variant(const B200GemmArgs* a, int sms, bool allow_workspace) {
     // idle and K is long (>= 6144): each split tile costs an fp32 partial written and
     // read back through L2 per CTA, a few microseconds that only a long K loop repays
     // (measured, 128-wide stream-K: 1024x1024x8192 f16 518 TFLOPS vs 396 for the best
-    // static tiling, e4m3 687 vs 636; 512x1024x8192 f16 319 vs 198, e4m3 375 vs 318).
+    // static tiling, e4m3 687 vs 636; 512x1024x8192 f16 317 vs 229, e4m3 373 vs 343).
     if (allow_workspace && pair_tiles * 4 <= pairs && a->K >= 6144) return B200_VARIANT_2CTA_STREAMK;
     // More than one wave (at the width pick_tile_n will choose): the persistent pairs
     // take their next tiles from cluster-launch-control work stealing (even with the

@@ -120,13 +120,14 @@ __host__ __device__ inline void tile_to_bmn(uint32_t tile, uint32_t num_bm, uint
   bn = t / gsize;
 }
 
-// K atoms per pipeline stage of the 256x256 and 256x128 pair tiles (1 or 2; compile-time
-// options so that a second build can compare them).
+// K atoms per pipeline stage of the 256x256 and 256x128 pair tiles (compile-time options
+// so that a second build can compare them; the stage count follows from the shared
+// memory left).
 #ifndef B200_PAIR_ATOMS_256
 #define B200_PAIR_ATOMS_256 2
 #endif
 #ifndef B200_PAIR_ATOMS_128
-#define B200_PAIR_ATOMS_128 2
+#define B200_PAIR_ATOMS_128 4
 #endif
 
 template <int AB, int CD, int CG, int SCHED, int TN>
@@ -138,10 +139,12 @@ struct GemmCfg {
   static constexpr int KIND = (AB == DT_E4M3) ? 1 : 0; // 0 kind::f16, 1 kind::f8f6f4
   static constexpr int AB_BYTES = (AB == DT_E4M3) ? 1 : 2;
   // One 128-byte swizzle atom of K per TMA box. A pair stage of one MMA width carries
-  // B200_PAIR_ATOMS_256 / _128 atoms (default two: one commit / barrier round trip per
-  // 8 MMAs instead of 4 keeps the tensor pipe busy, the per-stage commit costing
-  // tensor-pipe time); 1-CTA stages and 512-wide pair stages are already 48 KB and
-  // keep one atom so that four fit.
+  // B200_PAIR_ATOMS_256 / _128 atoms: two for 256x256 (64 KB, three stages) and four for
+  // 256x128 (96 KB, two stages). Fewer, larger stages mean fewer commit / barrier round
+  // trips per MMA, and each costs tensor-pipe time; the narrow tile's MMAs are half as
+  // long, so it gains from four atoms where the 256-wide tile loses with three (two
+  // 96 KB stages leave too little overlap for its longer stage). 1-CTA stages and
+  // 512-wide pair stages are already 48 KB and keep one atom so that four fit.
   static constexpr int ATOMS =
       (CG == 2 && NH == 1) ? (MMA_N == 128 ? B200_PAIR_ATOMS_128 : B200_PAIR_ATOMS_256) : 1;
   static constexpr int ATOM_K = 128 / AB_BYTES;        // elements of K per atom

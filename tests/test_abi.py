@@ -86,9 +86,9 @@ def test_variant_info(b200):
         info = b200.variant_info(v, b200.DT_BF16, tile_n=512)
         assert info["tile_m"] == 256 and info["tile_n"] == 512 and info["max_stages"] == 4
     for v in ("2cta", "2cta_clc", "2cta_streamk"):
-        # 256x128 pair tiles: two K atoms per stage, 48 KB, four stages
+        # 256x128 pair tiles: four K atoms per stage, 96 KB, two stages
         info = b200.variant_info(v, b200.DT_E4M3, tile_n=128)
-        assert info["tile_m"] == 256 and info["tile_n"] == 128 and info["max_stages"] == 4
+        assert info["tile_m"] == 256 and info["tile_n"] == 128 and info["max_stages"] == 2
     info = b200.variant_info("2cta_streamk", b200.DT_F16)
     assert info["tile_m"] == 256 and info["tile_n"] == 256 and info["max_stages"] == 3
     with pytest.raises(b200.B200Error):

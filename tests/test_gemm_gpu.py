@@ -97,9 +97,9 @@ def test_ref_check_fp8_512(b200, oracle, variant):
 @pytest.mark.parametrize("variant,stages", [("persistent", 2), ("persistent", 4), ("clc", 4),
                                             ("2cta", 2), ("2cta", 3), ("2cta_clc", 3),
                                             ("2cta_w", 2), ("2cta_w", 4), ("2cta_clc_w", 4),
-                                            ("2cta_n", 2), ("2cta_n", 4), ("2cta_clc_n", 4),
+                                            ("2cta_n", 2), ("2cta_clc_n", 2),
                                             ("2cta_streamk", 2), ("2cta_streamk", 3),
-                                            ("2cta_streamk_n", 4)])
+                                            ("2cta_streamk_n", 2)])
 def test_ref_check_fp8_persistent(b200, oracle, shape, group_m, variant, stages):
     """gemm_fp8_persist CHECK: seeds 1001/1002, single- and multi-wave, G in {1,8}."""
     M, N, K = shape
@@ -370,16 +370,18 @@ def test_streamk_split_tiles(b200, oracle, M, N, K, dtype, variant):
         assert np.array_equal(g, got[0])
 
 
-def _pick(b200, M, N, K, dtype=None):
+def _pick(b200, M, N, K, dtype=None, variant="auto", stages=0):
     a = b200.GemmArgs()
     a.ab_dtype = b200.DT_F16 if dtype is None else dtype
     a.c_dtype = b200.DT_F16 if a.ab_dtype != b200.DT_E4M3 else b200.DT_BF16
     a.M, a.N, a.K = M, N, K
     a.lda, a.ldb, a.ldc = K, K, N
     a.A, a.B, a.C = 0x10000, 0x20000, 0x30000
+    a.variant, a.stages = b200.VARIANTS[variant], stages
     v, tn = C.c_int32(), C.c_int32()
     assert b200.lib().b200_gemm_pick_config(C.byref(a), C.byref(v), C.byref(tn)) == 0
-    assert b200.lib().b200_gemm_pick_variant(C.byref(a)) == v.value
+    if variant == "auto":
+        assert b200.lib().b200_gemm_pick_variant(C.byref(a)) == v.value
     return b200.VARIANT_NAMES[v.value], tn.value
 
 
@@ -404,6 +406,25 @@ def test_auto_choice(b200):
     # M = 384 rounds up to two pair rows but three 1-CTA rows: 1-CTA needs fewer waves
     assert _pick(b200, 384, 65536, 1024) == ("persistent", 256)
     assert _pick(b200, 128, 1024, 1024) == ("1cta", 256)
+
+
+def test_tile_width_holds_explicit_stages(b200, oracle):
+    """tile_n = 0 with an explicit ring depth: the automatic width moves to the next wider
+    tile whose ring holds that many stages (the 256x128 pair ring is two deep), so a
+    request that the variant's tiles support never fails on the width choice."""
+    assert _pick(b200, 512, 512, 256, variant="2cta") == ("2cta", 128)
+    assert _pick(b200, 512, 512, 256, variant="2cta", stages=2) == ("2cta", 128)
+    assert _pick(b200, 512, 512, 256, variant="2cta", stages=3) == ("2cta", 256)
+    assert _pick(b200, 512, 512, 256, variant="2cta_clc", stages=4) == ("2cta_clc", 512)
+    assert _pick(b200, 512, 1024, 8192, variant="2cta_streamk") == ("2cta_streamk", 128)
+    assert _pick(b200, 512, 1024, 8192, variant="2cta_streamk", stages=3) == ("2cta_streamk", 256)
+    assert _pick(b200, 512, 1024, 8192, stages=3) == ("2cta_streamk", 256)
+    inp = make_inputs(oracle, 512, 512, 256, "f16", 601, 602)
+    ref = reference(oracle, inp)
+    for variant, stages in [("2cta", 3), ("2cta_clc", 4), ("2cta_streamk", 3)]:
+        for got in _run(b200, inp, variant, "f32", reps=1, stages=stages):
+            r = oracle.check_close(got, ref, 1e-3, 1e-3)
+            assert r.mismatches == 0, (variant, stages, r.max_abs_err)
 
 
 @pytest.mark.parametrize("variants", [("auto", "auto"), ("2cta_streamk", "2cta_streamk_n")])
