@@ -45,10 +45,12 @@ Measurement helpers (single GPU; the committed profiles/ summaries cite them):
   --mode power    <f16|bf16|e4m3> <config>...: sustained TFLOPS, energy per GEMM (NVML
                   total-energy counter), board power and SM clock under the power cap,
                   configurations interleaved in rounds; a config is `cublas` or
-                  `<variant>[:tile_n[:group_m]]`.
-  --mode sweep    [--dtypes f16,e4m3] [--shapes MxNxK,...]: launch time of every pair
-                  schedule and tile width and of cuBLASLt per shape (CUDA events,
-                  median of --steps launches), plus the library's AUTO choice.
+                  `<variant>[:tile_n[:group_m]][@ENV=V,...]` (environment set before each
+                  call, read by experimental builds only).
+  --mode sweep    [--dtypes f16,e4m3] [--shapes MxNxK,...] [config...]: launch time of
+                  every pair schedule and tile width (or of the configs given) and of
+                  cuBLASLt per shape (CUDA events, median of --steps launches), plus the
+                  library's AUTO choice.
 """
 from __future__ import annotations
 
@@ -720,6 +722,26 @@ def mode_profile(opt):
     print("ok", dt, who, variant, f"{M_}x{N_}x{K_}", tile_n)
 
 
+def _config_fn(b200, L, a, b, c, sa, sb, cf, stream):
+    """One launch of configuration `variant[:tile_n[:group_m]][@K=V,...]` (the environment
+    is set before each call, for experimental builds that read settings from it)."""
+    spec, _, env = cf.partition("@")
+    parts = spec.split(":")
+    args = b200.make_args(a, b, c, scale_a=sa, scale_b=sb, variant=parts[0],
+                          tile_n=int(parts[1]) if len(parts) > 1 else 0,
+                          group_m=int(parts[2]) if len(parts) > 2 else 0)
+
+    def ours():
+        for kv in filter(None, env.split(",")):
+            key, _, val = kv.partition("=")
+            os.environ[key] = val
+        rc = L.b200_gemm(C.byref(args), C.c_void_p(stream))
+        if rc != 0:
+            raise RuntimeError(b200.strerror(rc))
+
+    return ours
+
+
 def mode_power(opt):
     """Sustained TFLOPS, energy per GEMM, board power and SM clock under the power cap,
     configurations interleaved in rounds (slow thermal drift hits all of them alike)."""
@@ -739,21 +761,7 @@ def mode_power(opt):
         if cf == "cublas":
             fns[cf] = cublas
             continue
-        spec, _, env = cf.partition("@")  # "@K=V[,K=V]": environment for this config's calls
-        parts = spec.split(":")
-        args = b200.make_args(a, b, c, scale_a=sa, scale_b=sb, variant=parts[0],
-                              tile_n=int(parts[1]) if len(parts) > 1 else 0,
-                              group_m=int(parts[2]) if len(parts) > 2 else 0)
-
-        def ours(args=args, env=env):
-            for kv in filter(None, env.split(",")):
-                key, _, val = kv.partition("=")
-                os.environ[key] = val
-            rc = L.b200_gemm(C.byref(args), C.c_void_p(stream))
-            if rc != 0:
-                raise RuntimeError(b200.strerror(rc))
-
-        fns[cf] = ours
+        fns[cf] = _config_fn(b200, L, a, b, c, sa, sb, cf, stream)
     flop = 2.0 * M_ * N_ * K_
     res = {k: [] for k in fns}
     for r in range(opt.rounds):
@@ -822,18 +830,8 @@ def mode_sweep(opt):
                 for _ in range(20):
                     L.b200_gemm(C.byref(auto), C.c_void_p(stream))
                 torch.cuda.synchronize()
-            for cf in ["auto", "cublas"] + SWEEP_CONFIGS:
-                if cf == "cublas":
-                    fn = cublas
-                else:
-                    parts = cf.split(":")
-                    args = b200.make_args(a, b, c, scale_a=sa, scale_b=sb, variant=parts[0],
-                                          tile_n=int(parts[1]) if len(parts) > 1 else 0)
-
-                    def fn(args=args):
-                        rc = L.b200_gemm(C.byref(args), C.c_void_p(stream))
-                        if rc != 0:
-                            raise RuntimeError(b200.strerror(rc))
+            for cf in ["auto", "cublas"] + (opt.rest or SWEEP_CONFIGS):
+                fn = cublas if cf == "cublas" else _config_fn(b200, L, a, b, c, sa, sb, cf, stream)
                 try:
                     _, per = timed_loop(torch, fn, opt.steps, opt.warmup, torch.cuda.current_stream())
                     row[cf] = round(flop / (statistics.median(per) * 1e-3) / 1e12, 1)

@@ -92,14 +92,21 @@ constexpr uint64_t kDefaultWaitNs = 1000000000ull;  // 1 s per wait
 constexpr uint32_t kL2Policy = B200_L2_POLICY;
 
 // Experimental builds only (compiled with -DB200_EXPERIMENT_ENV, never by default):
-// the L2 policy bits and the operand maps' L2 promotion (128 or 256 bytes) come from
-// the environment variables B200_L2_POLICY and B200_L2_PROMO at every call, so that
-// bench.py --mode power can interleave cache settings inside one process.
+// the L2 policy bits, the operand maps' L2 promotion (128 or 256 bytes) and the L2
+// prefetch distance in k-blocks come from the environment variables B200_L2_POLICY,
+// B200_L2_PROMO and B200_PREFETCH_K at every call, so that bench.py --mode power and
+// --mode sweep can interleave these settings inside one process.
 uint32_t l2_policy_bits() {
 #ifdef B200_EXPERIMENT_ENV
   if (const char* e = std::getenv("B200_L2_POLICY")) return uint32_t(std::atoi(e));
 #endif
   return kL2Policy;
+}
+uint32_t prefetch_k_blocks(uint32_t dflt) {
+#ifdef B200_EXPERIMENT_ENV
+  if (const char* e = std::getenv("B200_PREFETCH_K")) return uint32_t(std::atoi(e));
+#endif
+  return dflt;
 }
 CUtensorMapL2promotion l2_promotion() {
 #ifdef B200_EXPERIMENT_ENV
@@ -396,6 +403,7 @@ int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status,
   kp.status = status;
   kp.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kDefaultWaitNs;
   kp.l2_policy = l2_policy_bits();
+  kp.prefetch_k = prefetch_k_blocks(0u);
   if (gather) {
     kp.gather = static_cast<const uint8_t*>(gather->dst);
     kp.gather_mode = gather->mode;

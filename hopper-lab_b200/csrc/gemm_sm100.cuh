@@ -77,6 +77,10 @@ struct KParams {
   // group-M group), bit 1 B loads evict_first (a B panel's reuse is within one wave),
   // bit 2 C stores evict_first (C is never read back); 0 = evict_normal everywhere
   uint32_t l2_policy;
+  // L2 prefetch distance in k-blocks (0 = off): with the loads of k-block kb the producer
+  // prefetches this CTA's boxes of k-block kb + prefetch_k into L2, so that a DRAM-streamed
+  // operand has more bytes in flight than the shared-memory ring holds
+  uint32_t prefetch_k;
   // SCHED_STREAMK only: fp32 partial-tile workspace (one 128 x MMA_N region per CTA
   // slot), per-slot ready flags, and this launch's epoch (the value a ready flag
   // holds; flags never need resetting between launches)
@@ -425,6 +429,25 @@ __global__ void __launch_bounds__(384, 1)
           const int32_t a_row = int32_t((bm * CG + rank) * Cfg::BM);
           // rows of this CTA's share of MMA h: bn*BN + h*MMA_N + rank*B_HALF_ROWS
           const int32_t b_row = int32_t(bn * Cfg::BN + rank * Cfg::B_HALF_ROWS);
+          // this CTA's boxes of k-block kb, into L2 only; boxes that reach past an edge
+          // of A or B are left to the loads
+          auto prefetch = [&](uint32_t kb) {
+#pragma unroll
+            for (int at = 0; at < Cfg::ATOMS; ++at) {
+              const uint32_t x = kb * Cfg::BK + at * Cfg::ATOM_K;
+              if (x + Cfg::ATOM_K > p.K) break;
+              if (uint32_t(a_row) + Cfg::BM <= p.M) tma_prefetch_2d(&tmA, int32_t(x), a_row);
+#pragma unroll
+              for (int h = 0; h < NH; ++h) {
+                const uint32_t r = uint32_t(b_row + h * Cfg::MMA_N);
+                if (r + Cfg::B_HALF_ROWS <= p.N) tma_prefetch_2d(&tmB, int32_t(x), int32_t(r));
+              }
+            }
+          };
+          if (p.prefetch_k) {
+            const uint32_t pend = min(cur.kb1, cur.kb0 + p.prefetch_k);
+            for (uint32_t kb = cur.kb0 + S; kb < pend; ++kb) prefetch(kb);
+          }
           for (uint32_t kb = cur.kb0; kb < cur.kb1; ++kb) {
             if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, p.wait_ns, abort_flag)) {
               fail(ST_PRODUCER_EMPTY);
@@ -459,6 +482,7 @@ __global__ void __launch_bounds__(384, 1)
                                    b_row + h * Cfg::MMA_N, lf, hint_b);
               }
             }
+            if (p.prefetch_k && kb + p.prefetch_k < cur.kb1) prefetch(kb + p.prefetch_k);
             ++issued;
             if (++stage == S) { stage = 0; phase ^= 1u; }
           }

@@ -257,6 +257,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* m, 
       : "memory");
 }
 
+// L2 prefetch of one box of a tiled tensor map: the TMA unit brings the box into L2
+// (no shared memory, no barrier), so a later load of it is an L2 hit.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* m, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(m), "r"(x), "r"(y)
+               : "memory");
+}
+
 // Pair form for cta_group::2: the data lands in this CTA's shared memory, the
 // completion bytes are credited to `bar`, which may be the leader CTA's barrier.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, int32_t x,

@@ -68,13 +68,18 @@ def _run(b200, inp, variant, out_dtype, reps=1, **kw):
 
 
 # ------------------------------------------------------------ reference CHECK blocks
-@pytest.mark.parametrize("variant", ALL_VARIANTS)
-@pytest.mark.parametrize("stages", [2, 3, 4])
+# Deepest shared-memory ring of each variant at its tile width (tile_n = 0: 256 wide);
+# test_ref_check_fp16_512 runs every depth from 2 up to it and checks the table against
+# b200_gemm_variant_info.
+RING = {"1cta": 4, "persistent": 4, "clc": 4, "2cta": 3, "2cta_clc": 3, "2cta_w": 4,
+        "2cta_clc_w": 4, "2cta_n": 2, "2cta_clc_n": 2, "2cta_streamk": 3, "2cta_streamk_n": 2}
+
+
+@pytest.mark.parametrize("variant,stages", [(v, s) for v in ALL_VARIANTS for s in range(2, RING[v] + 1)])
 def test_ref_check_fp16_512(b200, oracle, variant, stages):
     """gemm_ws CHECK: 512x512x256 fp16, seeds 601/602, fp32 C, 1e-3/1e-3, x3."""
     v, tn = _variant(variant)
-    if stages > b200.variant_info(v, tile_n=tn)["max_stages"]:
-        pytest.skip("deeper than this variant's shared-memory ring")
+    assert b200.variant_info(v, tile_n=tn)["max_stages"] == RING[variant]
     inp = make_inputs(oracle, 512, 512, 256, "f16", 601, 602)
     ref = reference(oracle, inp)
     for got in _run(b200, inp, variant, "f32", reps=3, stages=stages):
