@@ -95,16 +95,17 @@ constexpr uint32_t kL2Policy = B200_L2_POLICY;
 // the L2 policy bits, the operand maps' L2 promotion (128 or 256 bytes) and the L2
 // prefetch distance in k-blocks come from the environment variables B200_L2_POLICY,
 // B200_L2_PROMO and B200_PREFETCH_K at every call, so that bench.py --mode power and
-// --mode sweep can interleave these settings inside one process.
-uint32_t l2_policy_bits() {
+// --mode sweep can interleave these settings inside one process (an empty value keeps
+// the library's own choice).
+uint32_t l2_policy_bits(uint32_t dflt) {
 #ifdef B200_EXPERIMENT_ENV
-  if (const char* e = std::getenv("B200_L2_POLICY")) return uint32_t(std::atoi(e));
+  if (const char* e = std::getenv("B200_L2_POLICY"); e && *e) return uint32_t(std::atoi(e));
 #endif
-  return kL2Policy;
+  return dflt;
 }
 uint32_t prefetch_k_blocks(uint32_t dflt) {
 #ifdef B200_EXPERIMENT_ENV
-  if (const char* e = std::getenv("B200_PREFETCH_K")) return uint32_t(std::atoi(e));
+  if (const char* e = std::getenv("B200_PREFETCH_K"); e && *e) return uint32_t(std::atoi(e));
 #endif
   return dflt;
 }
@@ -266,6 +267,39 @@ uint32_t variant_smem(const VariantShape& vs, uint32_t stages) {
 
 int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// L2 prefetch distance and cache policy of a launch. With one or two block-rows of
+// tiles (M <= 512) each B panel is read by at most two tiles, so B streams from DRAM
+// about once and the shared-memory ring (two or three stages) holds too few bytes to
+// cover DRAM latency; prefetching each CTA's boxes two k-blocks ahead into L2 covers
+// it. With one or two block-columns (N <= 512 at 256-wide tiles) A is the streamed
+// operand, so the cache roles swap too (A evict_first, B evict_last). Measured on B200
+// (bench.py --mode power, sustained, cuBLASLt interleaved): 256x16384x8192 e4m3 1906 vs
+// 1728 TFLOPS (cuBLASLt 1820), f16 908 vs 902 (928); 16384x256x8192 e4m3 1950 vs 1730
+// (1903), f16 908 vs 907 (951). Launch-time sweeps: 512x8192x8192 f16 1232 vs 1148,
+// 8192x512x8192 f16 1234 vs 1188, 256x32768x4096 (work stealing, one block-row) f16 1074
+// vs 1010, e4m3 1844 vs 1743. Shapes with more block-rows and -columns, whose operands
+// are re-read from L2, lose with it (8192^3 f16 1277 vs 1505), so it stays off there.
+struct CachePlan {
+  uint32_t policy, prefetch_k;
+};
+constexpr uint32_t kPrefetchK = 2;
+constexpr uint32_t kL2PolicyStreamA = 4u | 8u | 16u;  // C first, A first, B last
+CachePlan cache_plan(int variant, uint32_t m_tiles, uint32_t n_tiles, int sms) {
+  CachePlan c{kL2Policy, 0u};
+  const bool one_wave = uint64_t(m_tiles) * n_tiles <= uint64_t(sms / 2);
+  if (variant == B200_VARIANT_2CTA && one_wave) {
+    if (m_tiles <= 2) {
+      c.prefetch_k = kPrefetchK;
+    } else if (n_tiles <= 2) {
+      c.prefetch_k = kPrefetchK;
+      c.policy = kL2PolicyStreamA;
+    }
+  } else if (variant == B200_VARIANT_2CTA_CLC && m_tiles == 1) {
+    c.prefetch_k = kPrefetchK;
+  }
+  return c;
+}
+
 // C columns per tile for a pair variant when the caller leaves tile_n = 0. Chosen from
 // launch-time sweeps on B200 (bench.py --mode sweep; medians of 30 launches):
 //   512: the 256x512 tile cuts operand traffic by a quarter (less energy per GEMM, so a
@@ -402,8 +436,9 @@ int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status,
   kp.scale_b = a.scale_b;
   kp.status = status;
   kp.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kDefaultWaitNs;
-  kp.l2_policy = l2_policy_bits();
-  kp.prefetch_k = prefetch_k_blocks(0u);
+  const CachePlan cp = cache_plan(variant, kp.m_tiles, kp.n_tiles, sms);
+  kp.l2_policy = l2_policy_bits(cp.policy);
+  kp.prefetch_k = prefetch_k_blocks(cp.prefetch_k);
   if (gather) {
     kp.gather = static_cast<const uint8_t*>(gather->dst);
     kp.gather_mode = gather->mode;

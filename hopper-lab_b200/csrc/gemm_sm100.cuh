@@ -75,7 +75,9 @@ struct KParams {
   uint64_t wait_ns;       // bound of every mbarrier wait
   // L2 cache policies: bit 0 A loads evict_last (A panels are reused by every wave of a
   // group-M group), bit 1 B loads evict_first (a B panel's reuse is within one wave),
-  // bit 2 C stores evict_first (C is never read back); 0 = evict_normal everywhere
+  // bit 2 C stores evict_first (C is never read back); the mirrored roles, for shapes
+  // whose A is the streamed operand: bit 3 A loads evict_first (when bit 0 is clear),
+  // bit 4 B loads evict_last (when bit 1 is clear); 0 = evict_normal everywhere
   uint32_t l2_policy;
   // L2 prefetch distance in k-blocks (0 = off): with the loads of k-block kb the producer
   // prefetches this CTA's boxes of k-block kb + prefetch_k into L2, so that a DRAM-streamed
@@ -415,8 +417,12 @@ __global__ void __launch_bounds__(384, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
-      const uint64_t hint_a = (p.l2_policy & 1u) ? policy_evict_last() : policy_evict_normal();
-      const uint64_t hint_b = (p.l2_policy & 2u) ? policy_evict_first() : policy_evict_normal();
+      const uint64_t hint_a = (p.l2_policy & 1u)   ? policy_evict_last()
+                              : (p.l2_policy & 8u) ? policy_evict_first()
+                                                   : policy_evict_normal();
+      const uint64_t hint_b = (p.l2_policy & 2u)    ? policy_evict_first()
+                              : (p.l2_policy & 16u) ? policy_evict_last()
+                                                    : policy_evict_normal();
       const uint32_t leader_full0 = (CG == 2) ? mapa_shared(bar_full, 0) : bar_full;
       if (!p.fault_inject) {
         WorkItem cur;

@@ -208,6 +208,26 @@ def test_config5_persistent_sweep(b200, oracle, M, N, K):
         assert not fails, (variant, fails)
 
 
+@pytest.mark.parametrize("dtype", ["f16", "e4m3"])
+@pytest.mark.parametrize("M,N,K", [(256, 16384, 8192), (512, 8192, 8192), (16384, 256, 8192),
+                                   (8192, 512, 8192), (256, 32768, 4096), (300, 9000, 1008),
+                                   (9000, 300, 1008)])
+def test_streamed_operand_shapes(b200, oracle, dtype, M, N, K):
+    """Shapes whose launches prefetch the streamed operand into L2 two k-blocks ahead of
+    the ring: one or two block-rows of tiles (B streamed), one or two block-columns (A
+    streamed, with the L2 cache roles swapped), and one block-row under work stealing.
+    The ragged cases end in boxes that reach past A, B or K, which the prefetch skips.
+    AUTO and the static pair; 256 seeded rows x all N and one full column slab against
+    the oracle."""
+    inp = make_inputs(oracle, M, N, K, dtype, 911, 912, scaled=(dtype == "e4m3"))
+    out = "bf16" if dtype == "e4m3" else "f16"
+    tol = TOL_E4M3 if dtype == "e4m3" else TOL_16
+    for variant in ["auto", "2cta"]:
+        (got,) = _run(b200, inp, variant, out)
+        fails = check_big(oracle, inp, got, tol, seed=6)
+        assert not fails, (variant, fails)
+
+
 # ------------------------------------------------------------------------- edge cases
 @pytest.mark.parametrize("variant", ALL_VARIANTS)
 @pytest.mark.parametrize("dtype,out", [("f16", "f16"), ("bf16", "bf16"), ("e4m3", "bf16"),
