@@ -324,9 +324,15 @@ int pick_tile_n(const B200GemmArgs* a, int variant, int sms) {
       variant != B200_VARIANT_2CTA_STREAMK)
     return 256;
   const int64_t pairs = sms / 2;
+  // A wider tile only where it pads N no more than the next narrower one: a 512-wide
+  // tile on N = 256 runs every MMA half on padding (32768x256x4096 f16 654 TFLOPS
+  // against cuBLASLt's 946 before this rule), and so does a 256-wide one on N <= 128.
+  const bool wide_ok = ceil_div(a->N, 512) * 2 == ceil_div(a->N, 256);
+  const bool narrow_only = a->N <= 128;
   int tn = 256;
   if (variant == B200_VARIANT_2CTA_STREAMK) tn = 128;
-  else if (a->K >= 1024 && ceil_div(a->M, 256) * ceil_div(a->N, 512) >= pairs) tn = 512;
+  else if (narrow_only) tn = 128;
+  else if (wide_ok && a->K >= 1024 && ceil_div(a->M, 256) * ceil_div(a->N, 512) >= pairs) tn = 512;
   else if (ceil_div(a->M, 256) * ceil_div(a->N, 256) * 2 <= pairs) tn = 128;
   if (a->stages > 0) {
     const int widest = (variant == B200_VARIANT_2CTA_STREAMK) ? 256 : 512;

@@ -102,7 +102,9 @@ typedef struct B200GemmArgs {
                               1-CTA variants: 256 only; pair variants: 128, 256, 512
                               (stream-K: 128 or 256). The default picks by wave count:
                               512 for K >= 1024 with a full wave of wide tiles, 128
-                              where 256-wide tiles would leave pairs idle, else 256;
+                              where 256-wide tiles would leave pairs idle or N <= 128,
+                              else 256; never a width that pads N more than the next
+                              narrower one;
                               with `stages` given, the next wider tile whose ring
                               holds that many stages                                    */
   int32_t reserved;        /* must be 0                                                  */

@@ -211,7 +211,7 @@ def test_config5_persistent_sweep(b200, oracle, M, N, K):
 @pytest.mark.parametrize("dtype", ["f16", "e4m3"])
 @pytest.mark.parametrize("M,N,K", [(256, 16384, 8192), (512, 8192, 8192), (16384, 256, 8192),
                                    (8192, 512, 8192), (256, 32768, 4096), (300, 9000, 1008),
-                                   (9000, 296, 1008)])
+                                   (9000, 296, 1008), (32768, 256, 4096), (16384, 128, 4096)])
 def test_streamed_operand_shapes(b200, oracle, dtype, M, N, K):
     """Shapes whose launches prefetch the streamed operand into L2 two k-blocks ahead of
     the ring: one or two block-rows of tiles (B streamed), one or two block-columns (A
@@ -430,6 +430,12 @@ def test_auto_choice(b200):
     assert _pick(b200, 8192, 8192, 512) == ("2cta_clc", 256)   # shorter K: double-buffered 256
     # M = 384 rounds up to two pair rows but three 1-CTA rows: 1-CTA needs fewer waves
     assert _pick(b200, 384, 65536, 1024) == ("persistent", 256)
+    # no width that pads N more than the next narrower one
+    assert _pick(b200, 32768, 256, 4096) == ("2cta_clc", 256)
+    assert _pick(b200, 32768, 768, 4096) == ("2cta_clc", 256)
+    assert _pick(b200, 32768, 1024, 4096) == ("2cta_clc", 512)
+    assert _pick(b200, 16384, 128, 4096) == ("2cta", 128)
+    assert _pick(b200, 32768, 128, 4096) == ("2cta_clc", 128)
     assert _pick(b200, 128, 1024, 1024) == ("1cta", 256)
 
 
