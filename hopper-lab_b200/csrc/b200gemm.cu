@@ -277,14 +277,17 @@ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // 1728 TFLOPS (cuBLASLt 1820), f16 908 vs 902 (928); 16384x256x8192 e4m3 1950 vs 1730
 // (1903), f16 908 vs 907 (951). Launch-time sweeps: 512x8192x8192 f16 1232 vs 1148,
 // 8192x512x8192 f16 1234 vs 1188, 256x32768x4096 (work stealing, one block-row) f16 1074
-// vs 1010, e4m3 1844 vs 1743. Shapes with more block-rows and -columns, whose operands
+// vs 1010, e4m3 1844 vs 1743; one block-column under work stealing, sustained:
+// 32768x256x4096 e4m3 1844 vs 1658 (cuBLASLt 1844), f16 894 vs 883 (947);
+// 32768x128x4096 e4m3 1252 vs 1064 (1208), f16 599 vs 566 (639). Shapes with more
+// block-rows and -columns, whose operands
 // are re-read from L2, lose with it (8192^3 f16 1277 vs 1505), so it stays off there.
 struct CachePlan {
   uint32_t policy, prefetch_k;
 };
 constexpr uint32_t kPrefetchK = 2;
 constexpr uint32_t kL2PolicyStreamA = 4u | 8u | 16u;  // C first, A first, B last
-CachePlan cache_plan(int variant, uint32_t m_tiles, uint32_t n_tiles, int sms) {
+CachePlan cache_plan(int variant, int tn, uint32_t m_tiles, uint32_t n_tiles, int sms) {
   CachePlan c{kL2Policy, 0u};
   const bool one_wave = uint64_t(m_tiles) * n_tiles <= uint64_t(sms / 2);
   if (variant == B200_VARIANT_2CTA && one_wave) {
@@ -296,6 +299,9 @@ CachePlan cache_plan(int variant, uint32_t m_tiles, uint32_t n_tiles, int sms) {
     }
   } else if (variant == B200_VARIANT_2CTA_CLC && m_tiles == 1) {
     c.prefetch_k = kPrefetchK;
+  } else if (variant == B200_VARIANT_2CTA_CLC && n_tiles == 1 && tn <= 256) {
+    c.prefetch_k = kPrefetchK;
+    c.policy = kL2PolicyStreamA;
   }
   return c;
 }
@@ -442,7 +448,7 @@ int gemm_prepare(const B200GemmArgs& a, int sms, int cc_major, uint32_t* status,
   kp.scale_b = a.scale_b;
   kp.status = status;
   kp.wait_ns = a.wait_limit_ns ? a.wait_limit_ns : kDefaultWaitNs;
-  const CachePlan cp = cache_plan(variant, kp.m_tiles, kp.n_tiles, sms);
+  const CachePlan cp = cache_plan(variant, vs.tn, kp.m_tiles, kp.n_tiles, sms);
   kp.l2_policy = l2_policy_bits(cp.policy);
   kp.prefetch_k = prefetch_k_blocks(cp.prefetch_k);
   if (gather) {

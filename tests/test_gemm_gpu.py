@@ -211,7 +211,8 @@ def test_config5_persistent_sweep(b200, oracle, M, N, K):
 @pytest.mark.parametrize("dtype", ["f16", "e4m3"])
 @pytest.mark.parametrize("M,N,K", [(256, 16384, 8192), (512, 8192, 8192), (16384, 256, 8192),
                                    (8192, 512, 8192), (256, 32768, 4096), (300, 9000, 1008),
-                                   (9000, 296, 1008), (32768, 256, 4096), (16384, 128, 4096)])
+                                   (9000, 296, 1008), (32768, 256, 4096), (16384, 128, 4096),
+                                   (32768, 128, 4096), (20000, 200, 1008)])
 def test_streamed_operand_shapes(b200, oracle, dtype, M, N, K):
     """Shapes whose launches prefetch the streamed operand into L2 two k-blocks ahead of
     the ring: one or two block-rows of tiles (B streamed), one or two block-columns (A
